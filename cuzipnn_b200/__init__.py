@@ -1,0 +1,18 @@
+"""B200-native ZipNN lossless tensor compression: the API of cuZipNN (ruihe774/cuZipNN,
+src/cuzipnn/__init__.py) on hand-written sm_100a kernels, with rANS as the entropy coder."""
+
+from ._codec import (
+    compress_tensor,
+    compress_tensor_with_crc32,
+    decompress_tensor,
+    hash_tensor_with_crc32,
+    last_decode_status,
+)
+
+__all__ = [
+    "compress_tensor",
+    "compress_tensor_with_crc32",
+    "decompress_tensor",
+    "hash_tensor_with_crc32",
+    "last_decode_status",
+]

@@ -1,0 +1,454 @@
+"""ZipNN on the B200: bit reordering, byte grouping and rANS coding in hand-written sm_100a kernels.
+
+This module keeps the public API, argument checks, device rules and blob container of the
+reference (ruihe774/cuZipNN, src/cuzipnn/_codec.py) and replaces its GPU pipeline (Triton split,
+nvCOMP ANS, a blocking host-side passthrough decision, table upload and two copy passes) with one
+call into libcuzipnn_b200.so per direction.
+
+Blob layout (little-endian, every section 8-byte aligned), as in src/cuzipnn/_codec.py:3-20:
+
+    0   magic "ZNNG" | u8 version | u8 dtype code | u8 ndim | u8 flags
+    8   u32 chunk_bytes | u32 n_comp
+    16  u64 numel
+    24  i64 shape[ndim]
+
+flags: bit 0 = exponent bit reordering, bit 1 = stored uncompressed.
+
+A stored blob (tensors smaller than min_compress_bytes) has chunk_bytes = n_comp = 0, and the
+header is followed directly by the tensor's bytes in row-major order.  Otherwise it continues:
+
+    ..  i32 stored_bytes[K * nch]  bytes stored for each (stream, chunk), rANS-coded or raw
+    ..  i32 comp_idx[n_comp]       indices of the rANS-coded chunks
+    ..  data                       chunks in (stream, chunk) order, each padded to 8 bytes
+
+The version byte is 3: coded chunks hold ZNR2 rANS payloads (see include/cuzipnn_b200.h), not
+nvCOMP ANS streams, so version-2 blobs of the reference are rejected, as the reference rejects
+other versions (src/cuzipnn/_codec.py:423-424).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import struct
+import zlib
+from collections.abc import Buffer
+
+import torch
+
+from . import _lib
+
+_MAGIC = b"ZNNG"
+_VERSION = 3
+_FIXED = struct.Struct("<4sBBBBIIQ")
+_FLAG_REORDER = 1
+_FLAG_STORED = 2
+_MAX_NDIM = 64
+MAX_CHUNK_BYTES = 1 << 24
+MIN_SUB_CHUNKS = 4
+MAX_SUB_CHUNKS = 64
+
+DEFAULT_CHUNK_BYTES = 128 * 1024
+DEFAULT_SUB_CHUNK_BYTES = 8 * 1024
+DEFAULT_PASSTHROUGH_THRESHOLD = 0.95
+DEFAULT_MIN_COMPRESS_BYTES = 64 * 1024
+DEFAULT_CHECKSUM_CHUNK_BYTES = 16 * 1024
+
+# src/cuzipnn/_codec.py:47-64
+_DTYPES = {
+    1: torch.bool,
+    2: torch.uint8,
+    3: torch.int8,
+    4: torch.int16,
+    5: torch.int32,
+    6: torch.int64,
+    7: torch.float16,
+    8: torch.bfloat16,
+    9: torch.float32,
+    10: torch.float64,
+    11: torch.float8_e4m3fn,
+    12: torch.float8_e5m2,
+    13: torch.uint16,
+    14: torch.uint32,
+    15: torch.uint64,
+    16: torch.complex64,
+}
+_CODES = {dtype: code for code, dtype in _DTYPES.items()}
+# As in ZipNN, only bfloat16 and float32 get the exponent bit reordering.
+_REORDER = {torch.bfloat16, torch.float32}
+
+
+def _align8(x: int) -> int:
+    return (x + 7) & ~7
+
+
+def _sub_chunks(chunk_bytes: int, sub_chunk_bytes: int) -> int:
+    """Sub-chunk count: chunk_bytes / sub_chunk_bytes rounded up to a power of 2 in [4, 64]
+    (src/cuzipnn/_codec.py:83-86)."""
+    count = 1 << (-(-chunk_bytes // sub_chunk_bytes) - 1).bit_length()
+    return min(max(count, MIN_SUB_CHUNKS), MAX_SUB_CHUNKS)
+
+
+def _layout(ndim: int, total: int, n_comp: int) -> tuple[int, int, int]:
+    """Offsets of the stored_bytes table, the comp_idx table and the data (_codec.py:89-93)."""
+    sizes_off = 24 + 8 * ndim
+    idx_off = sizes_off + 4 * total
+    data_off = _align8(idx_off + 4 * n_comp)
+    return sizes_off, idx_off, data_off
+
+
+def _check_device(compute_device: torch.device | str | None) -> torch.device | None:
+    """Validate compute_device without initializing CUDA (_codec.py:96-103)."""
+    if compute_device is None:
+        return None
+    device = torch.device(compute_device)
+    if device.type != "cuda":
+        raise ValueError(f"compute_device must be a CUDA device, not {device}")
+    return device
+
+
+def _gpu(x: torch.Tensor, compute_device: torch.device | None) -> torch.device:
+    """compute_device if given, else x's device if it is on the GPU, else the current CUDA device."""
+    device = compute_device
+    if device is None:
+        device = x.device if x.is_cuda else torch.device("cuda")
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    return device
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _crc32(data: torch.Tensor, checksum_chunk_bytes: int) -> torch.Tensor:
+    """Enqueue the CRC-32 of each checksum_chunk_bytes-byte chunk of `data`, a contiguous uint8
+    CUDA tensor (_codec.py:116-131).  The last chunk may be shorter.  Returns uint32 on the GPU."""
+    nbytes = data.numel()
+    m = -(-nbytes // checksum_chunk_bytes)
+    crc = torch.empty(m, dtype=torch.uint32, device=data.device)
+    if m:
+        tb = int(_lib.lib.zn_crc32_temp_bytes(nbytes, checksum_chunk_bytes))
+        temp = torch.empty(max(tb, 1), dtype=torch.uint8, device=data.device)
+        _lib.check(
+            _lib.lib.zn_crc32(
+                data.data_ptr(), nbytes, checksum_chunk_bytes, crc.data_ptr(), temp.data_ptr(), tb,
+                _stream(data.device),
+            ),
+            "zn_crc32",
+        )
+    return crc
+
+
+def _fill_stored(
+    blob: torch.Tensor, offset: int, x: torch.Tensor, checksum_chunk_bytes: int | None
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Copy x's bytes into blob[offset:], after the header.  With checksum_chunk_bytes the blob
+    is hashed on the CPU with zlib, as the reference does for these small blobs (_codec.py:134-147)."""
+    blob[offset:].view(x.dtype).view(x.shape).copy_(x)
+    if checksum_chunk_bytes is None:
+        return blob, None
+    data = memoryview((ctypes.c_char * blob.numel()).from_address(blob.data_ptr()))
+    crc = [
+        zlib.crc32(data[i : i + checksum_chunk_bytes])
+        for i in range(0, len(data), checksum_chunk_bytes)
+    ]
+    return blob, torch.tensor(crc, dtype=torch.uint32)
+
+
+def compress_tensor(
+    tensor: torch.Tensor,
+    *,
+    chunk_bytes: int = DEFAULT_CHUNK_BYTES,
+    sub_chunk_bytes: int = DEFAULT_SUB_CHUNK_BYTES,
+    passthrough_threshold: float = DEFAULT_PASSTHROUGH_THRESHOLD,
+    min_compress_bytes: int = DEFAULT_MIN_COMPRESS_BYTES,
+    pin_memory: bool = False,
+    compute_device: torch.device | str | None = None,
+    readback_to_cpu: bool = True,
+) -> torch.Tensor:
+    """Compress a tensor losslessly on the GPU; returns a 1-D uint8 tensor."""
+    blob, _ = _compress(
+        tensor,
+        chunk_bytes=chunk_bytes,
+        sub_chunk_bytes=sub_chunk_bytes,
+        passthrough_threshold=passthrough_threshold,
+        min_compress_bytes=min_compress_bytes,
+        checksum_chunk_bytes=None,
+        pin_memory=pin_memory,
+        compute_device=compute_device,
+        readback_to_cpu=readback_to_cpu,
+    )
+    return blob
+
+
+def compress_tensor_with_crc32(
+    tensor: torch.Tensor,
+    *,
+    chunk_bytes: int = DEFAULT_CHUNK_BYTES,
+    sub_chunk_bytes: int = DEFAULT_SUB_CHUNK_BYTES,
+    passthrough_threshold: float = DEFAULT_PASSTHROUGH_THRESHOLD,
+    min_compress_bytes: int = DEFAULT_MIN_COMPRESS_BYTES,
+    checksum_chunk_bytes: int = DEFAULT_CHECKSUM_CHUNK_BYTES,
+    pin_memory: bool = False,
+    compute_device: torch.device | str | None = None,
+    readback_to_cpu: bool = True,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """compress_tensor, plus the CRC-32 (as zlib.crc32) of each checksum_chunk_bytes-byte chunk
+    of the blob, the last one possibly shorter, as a 1-D uint32 tensor on the blob's device.
+
+    The blob is the same as compress_tensor's.  The checksums are computed on the GPU before the
+    blob is copied back (on the CPU for tensors below min_compress_bytes, which are stored
+    uncompressed); hash_tensor_with_crc32(blob) reproduces them, so a blob can be verified before
+    it is passed to decompress_tensor.
+    """
+    blob, checksums = _compress(
+        tensor,
+        chunk_bytes=chunk_bytes,
+        sub_chunk_bytes=sub_chunk_bytes,
+        passthrough_threshold=passthrough_threshold,
+        min_compress_bytes=min_compress_bytes,
+        checksum_chunk_bytes=checksum_chunk_bytes,
+        pin_memory=pin_memory,
+        compute_device=compute_device,
+        readback_to_cpu=readback_to_cpu,
+    )
+    assert checksums is not None
+    return blob, checksums
+
+
+def hash_tensor_with_crc32(
+    tensor: torch.Tensor,
+    *,
+    checksum_chunk_bytes: int = DEFAULT_CHECKSUM_CHUNK_BYTES,
+    compute_device: torch.device | str | None = None,
+    readback_to_cpu: bool = True,
+) -> torch.Tensor:
+    """CRC-32 (as zlib.crc32) of each checksum_chunk_bytes-byte chunk of the tensor's bytes in
+    row-major order, the last one possibly shorter, computed on the GPU.  Returns a 1-D uint32
+    tensor."""
+    if checksum_chunk_bytes <= 0:
+        raise ValueError("checksum_chunk_bytes must be positive")
+    x = tensor.detach()
+    device = _gpu(x, _check_device(compute_device))
+    with torch.cuda.device(device):
+        x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+        crc = _crc32(x.view(-1).view(torch.uint8), checksum_chunk_bytes)
+        return crc.cpu() if readback_to_cpu else crc
+
+
+def _header(tensor: torch.Tensor, flags: int, chunk_bytes: int, n_comp: int) -> bytes:
+    """The fixed header and shape (_codec.py:270-292)."""
+    fixed = _FIXED.pack(
+        _MAGIC, _VERSION, _CODES[tensor.dtype], tensor.dim(), flags, chunk_bytes, n_comp, tensor.numel()
+    )
+    return fixed + struct.pack(f"<{tensor.dim()}q", *tensor.shape)
+
+
+def _compress(
+    tensor: torch.Tensor,
+    *,
+    chunk_bytes: int,
+    sub_chunk_bytes: int,
+    passthrough_threshold: float,
+    min_compress_bytes: int,
+    checksum_chunk_bytes: int | None,
+    pin_memory: bool,
+    compute_device: torch.device | str | None,
+    readback_to_cpu: bool,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    # Argument checks in the reference's order and wording (_codec.py:243-262).
+    compute_device = _check_device(compute_device)
+    if pin_memory and not readback_to_cpu:
+        raise ValueError("pin_memory requires readback_to_cpu")
+    if tensor.dtype not in _CODES:
+        raise TypeError(f"unsupported dtype {tensor.dtype}")
+    if chunk_bytes % 8 or not 0 < chunk_bytes <= MAX_CHUNK_BYTES:
+        raise ValueError(f"chunk_bytes must be a multiple of 8 in (0, {MAX_CHUNK_BYTES}]")
+    if passthrough_threshold <= 0 or passthrough_threshold > 1:
+        raise ValueError("passthrough_threshold must be in (0, 1]")
+    if sub_chunk_bytes <= 0:
+        raise ValueError("sub_chunk_bytes must be positive")
+    if min_compress_bytes < 0:
+        raise ValueError("min_compress_bytes must be non-negative")
+    if checksum_chunk_bytes is not None and checksum_chunk_bytes <= 0:
+        raise ValueError("checksum_chunk_bytes must be positive")
+    sub_chunks = _sub_chunks(chunk_bytes, sub_chunk_bytes)
+    if tensor.dim() > _MAX_NDIM:
+        raise ValueError(f"at most {_MAX_NDIM} dimensions are supported")
+
+    x = tensor.detach()
+    k, n, reorder = x.element_size(), x.numel(), x.dtype in _REORDER
+    header_size = _FIXED.size + 8 * tensor.dim()
+
+    # Stored path and empty tensors (_codec.py:294-306): no GPU work with readback_to_cpu.
+    if n * k < min_compress_bytes or n == 0:
+        stored = n * k < min_compress_bytes
+        head = _header(tensor, _FLAG_STORED if stored else _FLAG_REORDER if reorder else 0,
+                       0 if stored else chunk_bytes, 0)
+        if readback_to_cpu:
+            blob = _populated_empty(header_size + n * k, pin_memory=pin_memory)
+            blob[:header_size].copy_(torch.frombuffer(bytearray(head), dtype=torch.uint8))
+            return _fill_stored(blob, header_size, x, checksum_chunk_bytes)
+        device = _gpu(x, compute_device)
+        with torch.cuda.device(device):
+            blob = torch.empty(header_size + n * k, dtype=torch.uint8, device=device)
+            blob[:header_size].copy_(torch.frombuffer(bytearray(head), dtype=torch.uint8))
+            blob[header_size:].view(x.dtype).view(x.shape).copy_(x)
+            crc = None if checksum_chunk_bytes is None else _crc32(blob, checksum_chunk_bytes)
+            return blob, crc
+
+    device = _gpu(x, compute_device)
+    with torch.cuda.device(device):
+        x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous().view(-1)
+        if x.data_ptr() % 16:
+            x = x.clone()
+        head = _header(tensor, _FLAG_REORDER if reorder else 0, chunk_bytes, 0)
+        cap = int(_lib.lib.zn_compress_bound(n, k, tensor.dim(), chunk_bytes))
+        temp_bytes = int(_lib.lib.zn_compress_temp_bytes(n, k, chunk_bytes, sub_chunks))
+        # The blob is packed into a buffer at least as large as the input (README "API").
+        out = torch.empty(cap, dtype=torch.uint8, device=device)
+        temp = torch.empty(max(temp_bytes, 1), dtype=torch.uint8, device=device)
+        size_dev = torch.empty(1, dtype=torch.int64, device=device)
+        _lib.check(
+            _lib.lib.zn_compress(
+                x.data_ptr(), n, k, int(reorder), head, len(head), chunk_bytes, sub_chunks,
+                float(passthrough_threshold), out.data_ptr(), cap, size_dev.data_ptr(),
+                temp.data_ptr(), temp_bytes, _stream(device),
+            ),
+            "zn_compress",
+        )
+        size = int(size_dev.item())
+        comp = out[:size]
+        crc = None
+        if checksum_chunk_bytes is not None:
+            crc = _crc32(comp, checksum_chunk_bytes)
+        if not readback_to_cpu:
+            return comp, crc
+        blob = _populated_empty(size, pin_memory=pin_memory)
+        # With a crc, crc.cpu() below syncs the stream, so blob is complete on return.
+        blob.copy_(comp, non_blocking=crc is not None)
+        return blob, None if crc is None else crc.cpu()
+
+
+def _parse_header(prefix: Buffer) -> tuple[torch.dtype, tuple[int, ...], int, int, int, int]:
+    """(_codec.py:416-428)"""
+    prefix = memoryview(prefix)
+    if len(prefix) < _FIXED.size:
+        raise ValueError("blob is too short")
+    magic, version, code, ndim, flags, chunk_bytes, n_comp, n = _FIXED.unpack_from(prefix)
+    if magic != _MAGIC or version != _VERSION or code not in _DTYPES:
+        raise ValueError("not a cuzipnn blob")
+    if len(prefix) < _FIXED.size + 8 * ndim:
+        raise ValueError("blob is too short")
+    shape = struct.unpack_from(f"<{ndim}q", prefix, _FIXED.size)
+    return _DTYPES[code], shape, flags, chunk_bytes, n_comp, n
+
+
+# Status word of the latest decompress_tensor call per device (0 = no decoding error).
+_LAST_STATUS: dict[int, torch.Tensor] = {}
+
+
+def last_decode_status(device: torch.device | str | int | None = None) -> int:
+    """Error bits the device kernels reported for the latest decompress_tensor on `device`
+    (synchronizes with it).  0 means every unit decoded and validated; nonzero means the blob was
+    malformed (the affected elements were zeroed).  decompress_tensor checks this itself when it
+    synchronizes anyway (readback_to_cpu=True)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    st = _LAST_STATUS.get(dev.index if dev.type == "cuda" else int(dev))
+    return 0 if st is None else int(st.item())
+
+
+def decompress_tensor(
+    blob: torch.Tensor,
+    *,
+    compute_device: torch.device | str | None = None,
+    readback_to_cpu: bool = False,
+) -> torch.Tensor:
+    """Decompress a blob produced by compress_tensor; the blob may be on the CPU or the GPU.
+
+    Passing a blob that is not from `compress_tensor` gives an unspecified result (never an
+    out-of-bounds access); last_decode_status() reports it.
+    """
+    compute_device = _check_device(compute_device)
+    if blob.dtype != torch.uint8 or blob.dim() != 1:
+        raise ValueError("blob must be a 1-D uint8 tensor")
+
+    blob = blob.detach()
+    prefix_len = min(blob.numel(), _FIXED.size + 8 * _MAX_NDIM)
+    prefix_tensor = blob[:prefix_len].to("cpu", memory_format=torch.contiguous_format).contiguous()
+    prefix = (ctypes.c_byte * prefix_len).from_address(prefix_tensor.data_ptr())
+    dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefix)
+    reorder = bool(flags & _FLAG_REORDER)
+
+    if flags & _FLAG_STORED:
+        # Stored uncompressed: copy the bytes after the header straight to the target device.
+        header_size = _FIXED.size + 8 * len(shape)
+        nbytes = math.prod(shape) * dtype.itemsize
+        if blob.numel() < header_size + nbytes:
+            raise ValueError("blob is truncated")
+        if readback_to_cpu:
+            out = _populated_empty(nbytes).view(dtype).view(shape)
+        else:
+            out = torch.empty(shape, dtype=dtype, device=_gpu(blob, compute_device))
+        out.view(-1).view(torch.uint8).copy_(blob[header_size : header_size + nbytes])
+        return out
+
+    if n == 0:
+        return torch.empty(
+            shape, dtype=dtype, device="cpu" if readback_to_cpu else _gpu(blob, compute_device)
+        )
+    if math.prod(shape) != n or chunk_bytes <= 0:
+        raise ValueError("not a cuzipnn blob")
+    device = _gpu(blob, compute_device)
+    out = torch.empty(shape, dtype=dtype, device=device)
+
+    k = out.element_size()
+    nch = -(-n // chunk_bytes)
+    total = k * nch
+    _, _, data_off = _layout(len(shape), total, n_comp)
+    if blob.numel() < data_off:
+        raise ValueError("blob is truncated")
+
+    with torch.cuda.device(device):
+        x = blob.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+        if x.data_ptr() % 8:
+            x = x.clone()
+        # A pinned blob is uploaded asynchronously, but the caller may reuse it once we return.
+        uploaded = torch.cuda.Event() if blob.is_pinned() else None
+        if uploaded is not None:
+            uploaded.record()
+        temp_bytes = int(_lib.lib.zn_decompress_temp_bytes(n, k, chunk_bytes))
+        temp = torch.empty(max(temp_bytes, 1), dtype=torch.uint8, device=device)
+        status = torch.zeros(1, dtype=torch.int32, device=device)
+        _lib.check(
+            _lib.lib.zn_decompress(
+                x.data_ptr(), x.numel(), n, k, int(reorder), len(shape), chunk_bytes, n_comp,
+                out.data_ptr(), status.data_ptr(), temp.data_ptr(), temp_bytes, _stream(device),
+            ),
+            "zn_decompress",
+        )
+        _LAST_STATUS[device.index] = status
+
+        if uploaded is not None:
+            uploaded.synchronize()
+
+        if readback_to_cpu:
+            src = out
+            out = _populated_empty(src.numel() * src.element_size()).view(src.dtype).view_as(src)
+            out.copy_(src)
+            if int(status.item()):
+                raise ValueError(f"blob is corrupt (decoder status {int(status.item())})")
+
+        return out
+
+
+def _populated_empty(size: int, *, pin_memory: bool = False) -> torch.Tensor:
+    """A CPU buffer whose pages are already faulted in (_codec.py:545-550)."""
+    t = torch.empty(size, dtype=torch.uint8, pin_memory=pin_memory)
+    if not pin_memory:
+        # There are other page sizes, but all >= 4KB.
+        t[::4096].fill_(1)
+    return t

@@ -1,0 +1,680 @@
+// Decompression: the fused whole-tensor path (zn_decompress) and the batched ANS seam
+// (zn_ans_decompress).
+//
+// zn_decompress replaces src/cuzipnn/_codec.py:471-530 (table upload, cumsum, nvCOMP ANS decode
+// into a planar buffer, then the Triton merge) with two kernels:
+//   1. dscan_kernel: one CTA turns the blob's stored_bytes and comp_idx tables into the blob
+//      offset of every (plane, chunk) unit, flags the rANS-coded ones and validates the tables.
+//   2. decode_kernel: one CTA per chunk.  It builds a 4096-entry decode table in shared memory for
+//      each coded plane, then each warp decodes 4 sub-chunks (8 lanes each, one shared word stream
+//      per sub-chunk), reads the raw planes of the same elements straight from the blob, merges
+//      the planes, reverts the exponent bit reorder and writes the elements.  There is no planar
+//      intermediate buffer.
+// Every blob access is bounds-checked; a malformed unit raises a bit in the status word and its
+// elements are zeroed.  No wait in these kernels depends on another thread's progress except
+// __syncthreads().
+#include "zn_common.cuh"
+
+namespace zn {
+namespace {
+
+constexpr int kDecThreads = 128;  // 4 warps per chunk
+constexpr int kChains = 1;        // rANS states per lane (sub-chunks per lane)
+constexpr int kSym = 256 / kDecThreads;  // symbols per thread in table building
+constexpr int64_t kCodedBit = int64_t(1) << 62;
+constexpr int64_t kOffMask = kCodedBit - 1;
+
+struct DecArgs {
+  // fused mode
+  const uint8_t* blob;
+  int64_t blob_bytes;
+  const int64_t* src;     // per unit: blob offset | kCodedBit, or -1 if invalid
+  int64_t sizes_off;
+  int64_t n, C, nch;
+  uint8_t* out;
+  int32_t* status;
+  // batched mode (K == 1): payload i at in_ptrs[i] (in_bytes[i]) decodes into out_ptrs[i]
+  const int64_t* in_ptrs;
+  const int64_t* in_bytes;
+  const int64_t* out_ptrs;
+  const int64_t* out_cap;
+  int32_t* statuses;
+  uint8_t* overflow;      // per chunk: more coded planes than the main pass holds
+};
+
+struct PlaneInfo {
+  const uint8_t* pl;  // payload (coded) or raw bytes of this unit's chunk
+  const uint8_t* lo;  // stream block loads may touch [lo, hi)
+  const uint8_t* hi;
+  int64_t size;
+  int coded;
+  int t;
+  int64_t states_off;
+  int64_t lens_off;        // per-state stream lengths
+  int lw;                  // bytes per length field
+  int32_t stream_off[64];  // halfword index of each sub-chunk's first (lane 0) stream
+};
+
+struct DecSmem {
+  uint32_t f[256];
+  uint32_t cum[256];
+  uint32_t red[8];
+  int err;
+  int t;
+  PlaneInfo p[8];
+};
+
+__device__ __forceinline__ uint32_t block_sum(uint32_t v, uint32_t* red) {
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  uint32_t s = 0;
+  for (int w = 0; w < kDecThreads / 32; ++w) s += red[w];
+  return s;
+}
+
+__device__ __forceinline__ uint32_t block_excl(uint32_t v, uint32_t* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint32_t incl = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  __syncthreads();
+  if (lane == 31) red[w] = incl;
+  __syncthreads();
+  uint32_t base = 0;
+  for (int q = 0; q < w; ++q) base += red[q];
+  return base + incl - v;
+}
+
+// Parse a ZNR2 payload header and build its decode table.  Entry of slot z (symbol s, cum c, freq
+// f): (f - 1) << 20 | s << 12 | (z - c), so the state update f * (x >> 12) + (z - c) is one IMAD
+// after the lookup.  Returns false (uniformly) if the payload is malformed.
+__device__ bool build_plane(PlaneInfo& P, int64_t m, uint32_t* tab, DecSmem& S) {
+  const int tid = threadIdx.x;
+  const uint8_t* pl = P.pl;
+  const int64_t size = P.size;
+  bool ok = size >= 34 && pl[0] >= kMinSubLog2 && pl[0] <= kMaxSubLog2 && pl[1] == 0;
+  if (!__syncthreads_and(ok)) return false;
+  const int t = pl[0];
+  uint32_t pres[kSym], f4[kSym];
+  uint32_t npres = 0;
+#pragma unroll
+  for (int h = 0; h < kSym; ++h) {
+    const int s = kSym * tid + h;
+    pres[h] = (pl[2 + (s >> 3)] >> (s & 7)) & 1;
+    npres += pres[h];
+  }
+  const uint32_t np = block_sum(npres, S.red);
+  const int64_t tb = table_bytes(int(np));
+  const Geom g = geom_of(m, t);
+  const int64_t mb = meta_bytes(int(np), g);
+  if (np == 0 || mb > size) return false;
+  uint32_t k = block_excl(npres, S.red);
+  uint32_t fsum = 0;
+#pragma unroll
+  for (int h = 0; h < kSym; ++h) {
+    f4[h] = 0;
+    if (pres[h]) {
+      const uint32_t bit = 12 * k++;
+      const uint8_t* q = pl + 34 + (bit >> 3);
+      const uint32_t v = (uint32_t(q[0]) | (uint32_t(q[1]) << 8) | (uint32_t(q[2]) << 16)) >> (bit & 7);
+      f4[h] = (v & 0xFFF) + 1;
+    }
+    fsum += f4[h];
+  }
+  const uint32_t total = block_sum(fsum, S.red);
+  if (total != kM) return false;
+  uint32_t c0 = block_excl(fsum, S.red);
+#pragma unroll
+  for (int h = 0; h < kSym; ++h) {
+    S.f[kSym * tid + h] = f4[h];
+    S.cum[kSym * tid + h] = c0;
+    c0 += f4[h];
+  }
+  // Per-sub-chunk stream offsets (sum of its 8 lane lengths; one warp, one sub-chunk per lane).
+  if (tid < 32) {
+    int64_t pos = mb / 2;
+    bool good = true;
+    for (int g0 = 0; g0 < g.nu; g0 += 32) {
+      const int gi = g0 + tid;
+      int64_t sub = 0;
+      if (gi < g.nu)
+        for (int l = 0; l < kLanes; ++l) {
+          const int64_t fi = int64_t(gi) * kLanes + l;
+          const int64_t nw = g.lw == 2 ? int64_t(pl[tb + 2 * fi]) | (int64_t(pl[tb + 2 * fi + 1]) << 8)
+                                       : int64_t(*reinterpret_cast<const uint32_t*>(pl + tb + 4 * fi));
+          good &= nw <= g.sc / kLanes;
+          sub += nw;
+        }
+      int64_t incl = sub;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (tid >= o) incl += v;
+      }
+      if (gi < g.nu) P.stream_off[gi] = int32_t(pos + incl - sub);
+      pos += __shfl_sync(0xFFFFFFFFu, incl, 31);
+    }
+    good = __all_sync(0xFFFFFFFFu, good);
+    if (tid == 0) {
+      P.t = t;
+      P.lens_off = tb;
+      P.lw = g.lw;
+      P.states_off = tb + lengths_bytes(g);
+      S.err = !(good && 2 * pos == size);
+    }
+  }
+  __syncthreads();
+  if (S.err) return false;
+  // Fill the slot table, one symbol per warp iteration, 32 slots per step.
+  const int lane = tid & 31, warp = tid >> 5;
+  for (int s = warp; s < 256; s += kDecThreads / 32) {
+    const uint32_t f = S.f[s], c = S.cum[s];
+    const uint32_t hi = ((f - 1) << 20) | (uint32_t(s) << 12);
+    for (uint32_t q = lane; q < f; q += 32) tab[c + q] = hi | q;
+  }
+  __syncthreads();
+  return true;
+}
+
+// One 16-byte block of a word stream.  Blocks wholly inside [lo, hi) are one 16-byte load; a block
+// that straddles the edge is read halfword by halfword (outside halfwords read as 0).
+__device__ __forceinline__ uint4 load_block(const uint8_t* gb, uint32_t q, const uint8_t* lo, const uint8_t* hi) {
+  const uint8_t* p = gb + 16 * uint64_t(q);
+  if (p >= lo && p + 16 <= hi) return __ldg(reinterpret_cast<const uint4*>(p));
+  uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int h = 0; h < 8; ++h) {
+    const uint8_t* q2 = p + 2 * h;
+    if (q2 >= lo && q2 + 2 <= hi) w[h >> 1] |= uint32_t(*reinterpret_cast<const uint16_t*>(q2)) << (16 * (h & 1));
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Decoder state of one rANS state (a lane of a sub-chunk) of one coded plane.  Stream positions
+// are halfword indices relative to the 16-byte aligned base gb of the payload.  Each state keeps
+// a ring of RH halfwords of its stream in shared memory: at every round start [ptr, ptr + 16) is
+// present (a round consumes at most 16 words) and up to two 16-byte blocks ahead are loaded, to
+// be stored at the round's end.
+struct Cursor {
+  uint32_t x, ptr, end, fill, nload;
+  uint4 r0, r1;
+};
+
+// Halfwords per ring: 64, or 32 when 8 coded planes share the shared memory.
+template <int KC>
+__host__ __device__ constexpr int ring_half() { return KC > 4 ? 32 : 64; }
+
+// One decode step of one state (symbol into byte (i & 3) of acc, next word read one step ahead).
+template <bool FULL, int RH, int I>
+__device__ __forceinline__ void decode_step(uint32_t& xv, uint32_t& pv, uint32_t& wn, uint32_t& acc, bool act,
+                                            const uint32_t* __restrict__ tab, const uint16_t* ring16) {
+  const uint32_t e = tab[xv & (kM - 1)];
+  const uint32_t q = xv >> kScaleBits;
+  uint32_t xn = (e >> 20) * q + (q + (e & 0xFFFu));
+  if (!FULL) xn = act ? xn : xv;
+  acc = __byte_perm(acc, e >> 12, (0x3210 & ~(0xF << (4 * (I & 3)))) | (4 << (4 * (I & 3))));
+  const bool need = (FULL || act) && xn < kL;
+  const uint32_t w = wn;
+  pv += need;
+  wn = ring16[pv & (RH - 1)];
+  xv = need ? __byte_perm(w, xn, 0x5410) : xn;  // (xn << 16) | w
+}
+
+// 16 steps of the lane's kChains states, interleaved so the independent chains overlap.  A stream
+// over-read is not tested per step: it leaves the final state or position wrong, which the caller
+// checks (ring reads are always in bounds).
+template <bool FULL, int RH>
+__device__ __forceinline__ void decode_round(Cursor* cb, const uint32_t* __restrict__ tab, const uint16_t* const* ring16,
+                                             const int* nact, uint32_t (*acc)[4]) {
+  uint32_t xv[kChains], pv[kChains], wn[kChains];
+#pragma unroll
+  for (int c = 0; c < kChains; ++c) {
+    xv[c] = cb[c].x;
+    pv[c] = cb[c].ptr;
+    wn[c] = ring16[c][pv[c] & (RH - 1)];
+  }
+#define ZN_STEP(I)                                                                                    \
+  _Pragma("unroll") for (int c = 0; c < kChains; ++c)                                                 \
+      decode_step<FULL, RH, I>(xv[c], pv[c], wn[c], acc[c][(I) >> 2], (I) < nact[c], tab, ring16[c]);
+  ZN_STEP(0) ZN_STEP(1) ZN_STEP(2) ZN_STEP(3) ZN_STEP(4) ZN_STEP(5) ZN_STEP(6) ZN_STEP(7)
+  ZN_STEP(8) ZN_STEP(9) ZN_STEP(10) ZN_STEP(11) ZN_STEP(12) ZN_STEP(13) ZN_STEP(14) ZN_STEP(15)
+#undef ZN_STEP
+#pragma unroll
+  for (int c = 0; c < kChains; ++c) {
+    cb[c].x = xv[c];
+    cb[c].ptr = pv[c];
+  }
+}
+
+// KC: coded planes per chunk held in shared memory.  The main pass (KC = 1 for K > 1) flags
+// chunks with more coded planes; a second pass with KC = K decodes only those.
+// Work split: a warp item is 8 sub-chunks; lane l of 8-lane segment g runs chain c on sub-chunk
+// 8 * item + 4 * c + g.
+template <int K, bool REORDER, int KC>
+__global__ void __launch_bounds__(kDecThreads) decode_kernel(DecArgs a, bool overflow_pass) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  constexpr int RH = ring_half<KC>();
+  uint32_t* tabs = reinterpret_cast<uint32_t*>(smem_raw);                      // [KC][4096]
+  uint4* rings = reinterpret_cast<uint4*>(smem_raw + KC * kM * 4);             // [KC][kChains][threads][RH / 8]
+  DecSmem& S = *reinterpret_cast<DecSmem*>(smem_raw + KC * kM * 4 + KC * kChains * kDecThreads * RH * 2);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t j = blockIdx.x;
+  if (overflow_pass && !a.overflow[j]) return;
+  const bool batched = a.in_ptrs != nullptr;
+  int64_t m;
+  uint8_t* outc;
+  if (batched) {
+    m = a.out_cap[j];
+    outc = reinterpret_cast<uint8_t*>(a.out_ptrs[j]);
+  } else {
+    m = min(a.C, a.n - j * a.C);
+    outc = a.out + j * a.C * K;
+  }
+  if (tid == 0) S.err = 0;
+  if (tid < K) {
+    PlaneInfo& P = S.p[tid];
+    if (batched) {
+      P.pl = reinterpret_cast<const uint8_t*>(a.in_ptrs[j]);
+      P.size = a.in_bytes[j];
+      P.coded = 1;
+      P.lo = P.pl;
+      P.hi = P.pl + P.size;
+    } else {
+      const int64_t u = int64_t(tid) * a.nch + j;
+      const int64_t s = a.src[u];
+      const int64_t stored = *reinterpret_cast<const int32_t*>(a.blob + a.sizes_off + 4 * u);
+      P.coded = s >= 0 && (s & kCodedBit);
+      P.pl = a.blob + (s & kOffMask);
+      P.size = stored;
+      P.lo = a.blob;
+      P.hi = a.blob + a.blob_bytes;
+      if (s < 0) atomicOr(&S.err, 1);
+    }
+    P.t = -1;
+  }
+  __syncthreads();
+  int ncoded = 0;
+  int pslot[KC];  // plane of each coded slot
+#pragma unroll
+  for (int q = 0; q < KC; ++q) pslot[q] = 0;
+  for (int b = 0; b < K; ++b)
+    if (S.p[b].coded) {
+      if (ncoded < KC) pslot[ncoded] = b;
+      ++ncoded;
+    }
+  if (KC < K && !overflow_pass) {
+    const bool over = ncoded > KC;
+    if (tid == 0) a.overflow[j] = over;
+    if (over) return;
+  }
+  bool bad = S.err != 0 || m <= 0;
+  for (int q = 0; q < KC && q < ncoded && !bad; ++q)
+    if (!build_plane(S.p[pslot[q]], m, tabs + q * kM, S)) bad = true;
+  int t = 4;
+  if (!bad && ncoded) {
+    t = S.p[pslot[0]].t;
+    // All coded planes of a chunk must share one sub-chunk geometry.
+    for (int q = 0; q < KC && q < ncoded; ++q)
+      if (S.p[pslot[q]].t != t) bad = true;
+  }
+  if (bad) {
+    if (tid == 0) {
+      if (batched) a.statuses[j] = kErrPayload;
+      else atomicOr(a.status, kErrPayload);
+    }
+    if (m > 0)
+      for (int64_t i = tid; i < m * K; i += kDecThreads) outc[i] = 0;
+    return;
+  }
+
+  const Geom g = geom_of(m, t);
+  const int seg = lane >> 3, l = lane & 7;
+  const int rounds = int(g.sc / kRound);
+  const bool out16 = (reinterpret_cast<uintptr_t>(outc) & 15) == 0;
+  bool coded[K];
+  const uint8_t* src[K];
+#pragma unroll
+  for (int b = 0; b < K; ++b) {
+    coded[b] = S.p[b].coded;
+    src[b] = S.p[b].pl;
+  }
+  const uint8_t* gb[KC];
+  const uint8_t* lo[KC];
+  const uint8_t* hi[KC];
+#pragma unroll
+  for (int q = 0; q < KC; ++q) {
+    gb[q] = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(S.p[pslot[q]].pl) & ~uintptr_t(15));
+    lo[q] = S.p[pslot[q]].lo;
+    hi[q] = S.p[pslot[q]].hi;
+  }
+  bool err = false;
+  const int items = int(cdiv(g.nu, 4 * kChains));
+  for (int item = warp; item < items; item += kDecThreads / 32) {
+    int gi[kChains];
+    int64_t base[kChains], len[kChains];
+    bool valid[kChains];
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) {
+      gi[c] = 4 * kChains * item + 4 * c + seg;
+      valid[c] = gi[c] < g.nu;
+      base[c] = int64_t(gi[c]) * g.sc;
+      len[c] = valid[c] ? min(g.sc, m - base[c]) : 0;
+    }
+    Cursor cur[KC][kChains];
+    const uint16_t* ring16[KC][kChains];
+#pragma unroll
+    for (int q = 0; q < KC; ++q)
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) {
+        Cursor& cb = cur[q][c];
+        ring16[q][c] = reinterpret_cast<const uint16_t*>(rings + ((q * kChains + c) * kDecThreads + tid) * (RH / 8));
+        cb.x = kL;
+        cb.ptr = cb.end = cb.fill = cb.nload = 0;
+        if (q < ncoded && valid[c]) {
+          const PlaneInfo& P = S.p[pslot[q]];
+          const int64_t fbase = int64_t(gi[c]) * kLanes;
+          uint32_t before = 0, mine = 0;
+          for (int ll = 0; ll <= l; ++ll) {
+            const int64_t fi = fbase + ll;
+            const uint32_t nw = P.lw == 2 ? *reinterpret_cast<const uint16_t*>(P.pl + P.lens_off + 2 * fi)
+                                          : *reinterpret_cast<const uint32_t*>(P.pl + P.lens_off + 4 * fi);
+            if (ll < l) before += nw;
+            else mine = nw;
+          }
+          const uint32_t h0 = uint32_t((P.pl - gb[q]) >> 1) + uint32_t(P.stream_off[gi[c]]) + before;
+          cb.x = *reinterpret_cast<const uint32_t*>(P.pl + P.states_off + 4 * (fbase + l));
+          cb.ptr = h0;
+          cb.end = h0 + mine;
+          cb.fill = h0 & ~7u;
+          err |= cb.x < kL;
+        }
+      }
+    for (int r = 0; r < rounds; ++r) {
+      int nact[kChains];
+      int64_t off[kChains];
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) {
+        off[c] = int64_t(r) * kRound + l * kSteps;
+        nact[c] = int(max(int64_t(0), min(int64_t(kSteps), len[c] - off[c])));
+      }
+      // Ring upkeep: make [ptr, ptr + 16) present, start up to two block loads ahead.
+#pragma unroll
+      for (int q = 0; q < KC; ++q) {
+        if (q >= ncoded) break;
+#pragma unroll
+        for (int c = 0; c < kChains; ++c) {
+          Cursor& cb = cur[q][c];
+          uint4* ring = const_cast<uint4*>(reinterpret_cast<const uint4*>(ring16[q][c]));
+          const uint32_t end8 = (cb.end + 7) & ~7u;
+          const uint32_t need = min((cb.ptr + 16 + 7) & ~7u, end8);
+          while (cb.fill < need) {
+            ring[(cb.fill / 8) & (RH / 8 - 1)] = load_block(gb[q], cb.fill / 8, lo[q], hi[q]);
+            cb.fill += 8;
+          }
+          const uint32_t limit = min((cb.ptr + RH) & ~7u, end8);
+          cb.nload = limit > cb.fill ? min((limit - cb.fill) / 8, 2u) : 0u;
+          if (cb.nload > 0) cb.r0 = load_block(gb[q], cb.fill / 8, lo[q], hi[q]);
+          if (cb.nload > 1) cb.r1 = load_block(gb[q], cb.fill / 8 + 1, lo[q], hi[q]);
+        }
+      }
+      uint32_t p[kChains][K][4];
+#pragma unroll
+      for (int c = 0; c < kChains; ++c)
+#pragma unroll
+        for (int b = 0; b < K; ++b) {
+          if (coded[b]) continue;
+          const uint8_t* sp = src[b] + base[c] + off[c];
+          if (nact[c] == 16) {
+            const uint2 v0 = reinterpret_cast<const uint2*>(sp)[0], v1 = reinterpret_cast<const uint2*>(sp)[1];
+            p[c][b][0] = v0.x; p[c][b][1] = v0.y; p[c][b][2] = v1.x; p[c][b][3] = v1.y;
+          } else {
+            uint64_t vlo = 0, vhi = 0;
+            for (int i = 0; i < nact[c]; ++i) {
+              const uint64_t byte = sp[i];
+              if (i < 8) vlo |= byte << (8 * i);
+              else vhi |= byte << (8 * (i - 8));
+            }
+            p[c][b][0] = uint32_t(vlo); p[c][b][1] = uint32_t(vlo >> 32);
+            p[c][b][2] = uint32_t(vhi); p[c][b][3] = uint32_t(vhi >> 32);
+          }
+        }
+      const bool full = nact[0] == kSteps && nact[kChains - 1] == kSteps;
+#pragma unroll
+      for (int q = 0; q < KC; ++q) {
+        if (q >= ncoded) break;
+        uint32_t acc[kChains][4] = {};
+        if (full) decode_round<true, RH>(cur[q], tabs + q * kM, ring16[q], nact, acc);
+        else decode_round<false, RH>(cur[q], tabs + q * kM, ring16[q], nact, acc);
+#pragma unroll
+        for (int c = 0; c < kChains; ++c)
+#pragma unroll
+          for (int b = 0; b < K; ++b)
+            if (b == pslot[q]) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) p[c][b][i] = acc[c][i];
+            }
+      }
+      // Store the blocks loaded at the round's start (this round's reads are done).
+#pragma unroll
+      for (int q = 0; q < KC; ++q) {
+        if (q >= ncoded) break;
+#pragma unroll
+        for (int c = 0; c < kChains; ++c) {
+          Cursor& cb = cur[q][c];
+          uint4* ring = const_cast<uint4*>(reinterpret_cast<const uint4*>(ring16[q][c]));
+          if (cb.nload > 0) ring[(cb.fill / 8) & (RH / 8 - 1)] = cb.r0;
+          if (cb.nload > 1) ring[(cb.fill / 8 + 1) & (RH / 8 - 1)] = cb.r1;
+          cb.fill += 8 * cb.nload;
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) {
+        if (nact[c] <= 0) continue;
+        uint32_t e[4 * K];
+        planes_to_elements<K>(p[c], e);
+        reorder_words<K, REORDER, false>(e, 4 * K);
+        uint8_t* dst = outc + (base[c] + off[c]) * K;
+        if (nact[c] == 16) {
+          store_words(dst, e, 4 * K, out16 && ((((base[c] + off[c]) * K) & 15) == 0));
+        } else {
+#pragma unroll
+          for (int w = 0; w < 4 * K; ++w)
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq)
+              if (4 * w + qq < nact[c] * K) dst[4 * w + qq] = uint8_t(e[w] >> (8 * qq));
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < KC; ++q)
+#pragma unroll
+      for (int c = 0; c < kChains; ++c)
+        if (q < ncoded && valid[c]) err |= (cur[q][c].x != kL) || (cur[q][c].ptr != cur[q][c].end);
+  }
+  if (__syncthreads_or(err) && tid == 0) {
+    if (batched) a.statuses[j] = kErrStream;
+    else atomicOr(a.status, kErrStream);
+  } else if (batched && tid == 0) {
+    a.statuses[j] = 0;
+  }
+}
+
+// ---- table scan (src/cuzipnn/_codec.py:492-496, 529) ----------------------------------------
+
+constexpr int kScanThreads = 1024;
+
+struct DScanArgs {
+  const uint8_t* blob;
+  int64_t blob_bytes;
+  int64_t total, nch, C, n;
+  int64_t sizes_off, idx_off, n_comp, data_off;
+  int64_t* src;
+  int32_t* status;
+};
+
+__global__ void __launch_bounds__(kScanThreads) dscan_kernel(DScanArgs a) {
+  __shared__ int64_t sm[64];
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int64_t last = a.n - (a.nch - 1) * a.C;
+  const int32_t* stored = reinterpret_cast<const int32_t*>(a.blob + a.sizes_off);
+  int64_t carry = a.data_off;
+  bool bad = false;
+  for (int64_t start = 0; start < a.total; start += kScanThreads) {
+    const int64_t i = start + tid;
+    int64_t v = 0;
+    if (i < a.total) {
+      const int64_t s = stored[i];
+      bad |= s < 0;
+      v = s < 0 ? 0 : align8(s);
+    }
+    int64_t incl = v;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += u;
+    }
+    if (lane == 31) sm[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+      int64_t q = sm[lane];
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t u = __shfl_up_sync(0xFFFFFFFFu, q, o);
+        if (lane >= o) q += u;
+      }
+      sm[32 + lane] = q;
+    }
+    __syncthreads();
+    const int64_t excl = carry + (w ? sm[32 + w - 1] : 0) + incl - v;
+    if (i < a.total) a.src[i] = excl;
+    carry += sm[32 + 31];
+    __syncthreads();
+  }
+  __syncthreads();
+  const int32_t* idx = reinterpret_cast<const int32_t*>(a.blob + a.idx_off);
+  for (int64_t q = tid; q < a.n_comp; q += kScanThreads) {
+    const int64_t i = idx[q];
+    if (i < 0 || i >= a.total) { bad = true; continue; }
+    a.src[i] |= kCodedBit;
+  }
+  __syncthreads();
+  for (int64_t i = tid; i < a.total; i += kScanThreads) {
+    const int64_t s = a.src[i];
+    const int64_t off = s & kOffMask, st = stored[i];
+    const int64_t raw = (i % a.nch) == a.nch - 1 ? last : a.C;
+    const bool coded = s & kCodedBit;
+    // A raw unit holds exactly the chunk's bytes; a coded one must lie inside the blob.
+    if (st < 0 || off + st > a.blob_bytes || (!coded && st != raw)) {
+      a.src[i] = -1;
+      bad = true;
+    }
+  }
+  if (__syncthreads_or(bad) && tid == 0) atomicOr(a.status, kErrTable);
+}
+
+size_t dec_smem(int KC) {
+  return size_t(KC) * kM * 4 + size_t(KC) * kChains * kDecThreads * (KC > 4 ? 32 : 64) * 2 + sizeof(DecSmem);
+}
+
+template <int K, bool REORDER, int KC>
+int launch_decode_pass(const DecArgs& a, int64_t grid, bool overflow_pass, cudaStream_t s) {
+  const size_t sm = dec_smem(KC);
+  auto fn = decode_kernel<K, REORDER, KC>;
+  if (int rc = set_max_smem(reinterpret_cast<const void*>(fn), int(sm))) return rc;
+  fn<<<unsigned(grid), kDecThreads, sm, s>>>(a, overflow_pass);
+  count_launch();
+  return check_launch("decode_kernel");
+}
+
+// Main pass with one coded plane per chunk in shared memory, then (K > 1) the overflow pass.
+template <int K, bool REORDER>
+int launch_decode(const DecArgs& a, int64_t grid, cudaStream_t s) {
+  if (int rc = launch_decode_pass<K, REORDER, 1>(a, grid, false, s)) return rc;
+  if constexpr (K > 1) return launch_decode_pass<K, REORDER, K>(a, grid, true, s);
+  return ZN_OK;
+}
+
+}  // namespace
+}  // namespace zn
+
+using namespace zn;
+
+extern "C" {
+
+size_t zn_ans_decompress_temp_bytes(int64_t count) { (void)count; return 0; }
+
+int zn_ans_decompress(const int64_t* in_ptrs, const int64_t* in_bytes, const int64_t* out_capacity, int64_t count,
+                      const int64_t* out_ptrs, int32_t* statuses, void* temp, size_t temp_bytes, void* stream) {
+  (void)temp;
+  (void)temp_bytes;
+  if (count < 0 || count > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_ans_decompress: bad arguments");
+  if (count == 0) return ZN_OK;
+  DecArgs a{};
+  a.in_ptrs = in_ptrs;
+  a.in_bytes = in_bytes;
+  a.out_ptrs = out_ptrs;
+  a.out_cap = out_capacity;
+  a.statuses = statuses;
+  a.nch = count;
+  return launch_decode<1, false>(a, count, static_cast<cudaStream_t>(stream));
+}
+
+size_t zn_decompress_temp_bytes(int64_t n, int k, int64_t chunk_bytes) {
+  if (n < 0 || k <= 0 || chunk_bytes <= 0) return 0;
+  const int64_t nch = cdiv(n, chunk_bytes);
+  return size_t(int64_t(k) * nch) * 8 + size_t(nch);  // unit offsets, then per-chunk overflow flags
+}
+
+int zn_decompress(const void* blob, int64_t blob_bytes, int64_t n, int k, int reorder, int ndim, int64_t chunk_bytes,
+                  int64_t n_comp, void* out, int32_t* status, void* temp, size_t temp_bytes, void* stream) {
+  if (n < 0 || (k != 1 && k != 2 && k != 4 && k != 8) || (reorder && k != 2 && k != 4) || chunk_bytes <= 0 ||
+      ndim < 0 || ndim > 64 || n_comp < 0 || (reinterpret_cast<uintptr_t>(blob) & 7))
+    return set_error(ZN_ERR_INVALID, "zn_decompress: bad arguments");
+  if (n == 0) return ZN_OK;
+  const int64_t nch = cdiv(n, chunk_bytes), total = int64_t(k) * nch;
+  if (nch > 0x7FFFFFFF || n_comp > total) return set_error(ZN_ERR_INVALID, "zn_decompress: bad tables");
+  const int64_t sizes_off = 24 + 8 * int64_t(ndim), idx_off = sizes_off + 4 * total;
+  const int64_t data_off = align8(idx_off + 4 * n_comp);
+  if (blob_bytes < data_off) return set_error(ZN_ERR_INVALID, "zn_decompress: blob is truncated");
+  if (!temp || temp_bytes < size_t(total) * 8 + size_t(nch))
+    return set_error(ZN_ERR_SPACE, "zn_decompress: temp buffer too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DScanArgs sa{};
+  sa.blob = static_cast<const uint8_t*>(blob);
+  sa.blob_bytes = blob_bytes;
+  sa.total = total;
+  sa.nch = nch;
+  sa.C = chunk_bytes;
+  sa.n = n;
+  sa.sizes_off = sizes_off;
+  sa.idx_off = idx_off;
+  sa.n_comp = n_comp;
+  sa.data_off = data_off;
+  sa.src = static_cast<int64_t*>(temp);
+  sa.status = status;
+  dscan_kernel<<<1, kScanThreads, 0, s>>>(sa);
+  count_launch();
+  if (int rc = check_launch("dscan_kernel")) return rc;
+  DecArgs a{};
+  a.blob = sa.blob;
+  a.blob_bytes = blob_bytes;
+  a.src = sa.src;
+  a.sizes_off = sizes_off;
+  a.n = n;
+  a.C = chunk_bytes;
+  a.nch = nch;
+  a.out = static_cast<uint8_t*>(out);
+  a.status = status;
+  a.overflow = static_cast<uint8_t*>(temp) + size_t(total) * 8;
+  switch (k * 2 + (reorder ? 1 : 0)) {
+    case 2: return launch_decode<1, false>(a, nch, s);
+    case 4: return launch_decode<2, false>(a, nch, s);
+    case 5: return launch_decode<2, true>(a, nch, s);
+    case 8: return launch_decode<4, false>(a, nch, s);
+    case 9: return launch_decode<4, true>(a, nch, s);
+    default: return launch_decode<8, false>(a, nch, s);
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,1089 @@
+// Compression: the fused whole-tensor path (zn_compress) and the batched ANS seam
+// (zn_ans_compress).
+//
+// zn_compress replaces src/cuzipnn/_codec.py:308-413 (split, nvCOMP ANS, host passthrough
+// decision and table build, two copy passes, prefix upload) with three kernels and no host round
+// trip:
+//   1. encode_kernel: one CTA per chunk.  It streams the chunk's elements once to build the
+//      histograms of all K byte planes (shared-memory atomics, 16 lane-private columns), turns
+//      each into a ZNR2 frequency table, and rANS-encodes every plane that can still come out
+//      below the passthrough budget into a scratch slot.  A plane whose entropy lower bound is
+//      already at or above the budget is skipped (it would be stored raw anyway).
+//   2. scan_kernel: one CTA applies the passthrough rule of _codec.py:361-372, writes the header,
+//      the stored_bytes and comp_idx tables, and the destination of every unit.
+//   3. pack_kernel: one CTA per chunk re-reads the chunk (in reverse order, so the most recently
+//      encoded chunks are still in L2), writes raw planes straight from the elements and copies
+//      the coded payloads from scratch, zero-padding every unit to 8 bytes.
+#include <math.h>
+
+#include "zn_common.cuh"
+
+namespace zn {
+namespace {
+
+constexpr int kEncThreads = 128;  // 4 warps per chunk
+constexpr int kEncSym = 256 / kEncThreads;  // symbols per thread in table building
+constexpr int kEncChains = 1;  // rANS states per lane (sub-chunks per lane)
+static_assert(kEncChains == 1, "the staging ring holds one state per lane");
+constexpr int kCols = 16;  // lane-private histogram columns
+
+struct EncArgs {
+  const uint8_t* x;         // fused: tensor elements
+  const int64_t* in_ptrs;   // batched: chunk addresses (K == 1), else null
+  const int64_t* in_bytes;  // batched: chunk sizes
+  int64_t n;                // fused: element count
+  int64_t C;                // elements per chunk
+  int64_t nch;              // chunks (units per plane)
+  int t;                    // log2(sub-chunks)
+  double threshold;         // passthrough threshold (batched: skipping disabled)
+  bool allow_skip;
+  uint8_t* meta;            // per unit, meta_slot bytes
+  int64_t meta_slot;
+  uint16_t* streams;        // per unit: unit_words words; per sub-chunk: sub_words; per lane: lane_words
+  int64_t unit_words;
+  int64_t sub_words;
+  int64_t lane_words;
+  int32_t* comp_bytes;      // per unit: payload bytes, or -1 if not coded
+  const uint32_t* part_hist;  // [nch][kHistParts][K][256] partial histograms from hist_kernel
+};
+
+// Parts per chunk of the histogram kernel: a chunk's histogram is built by kHistParts CTAs, so
+// the chunk is read at the full memory bandwidth rather than by one CTA.
+constexpr int kHistParts = 8;
+constexpr int kHistThreads = 256;
+
+struct EncSmem {
+  uint32_t f[256];
+  uint32_t fbuf[96];        // 256 12-bit fields
+  uint32_t red_u[8];
+  float red_f[8];
+  unsigned long long red_ull[8];
+  int npl[8];
+  int skip[8];
+  int nwsum[8];             // stream words per plane
+  uint4 stage[kEncThreads][4];  // per lane: last 32 emitted words, flushed in 16-byte blocks
+};
+
+// ---- block-wide helpers (kEncThreads = 128 threads = 4 warps) ----------------------------------
+
+__device__ __forceinline__ uint32_t block_sum_u(uint32_t v, uint32_t* red) {
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  uint32_t s = 0;
+  for (int w = 0; w < kEncThreads / 32; ++w) s += red[w];
+  return s;
+}
+
+__device__ __forceinline__ float block_sum_f(float v, float* red) {
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int w = 0; w < kEncThreads / 32; ++w) s += red[w];
+  return s;
+}
+
+__device__ __forceinline__ unsigned long long block_max_ull(unsigned long long v, unsigned long long* red) {
+  for (int o = 16; o; o >>= 1) {
+    unsigned long long u = __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    v = u > v ? u : v;
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  unsigned long long s = 0;
+  for (int w = 0; w < kEncThreads / 32; ++w) s = red[w] > s ? red[w] : s;
+  return s;
+}
+
+// Exclusive scan of one value per thread over the block.
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint32_t incl = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  __syncthreads();
+  if (lane == 31) red[w] = incl;
+  __syncthreads();
+  uint32_t base = 0;
+  for (int q = 0; q < w; ++q) base += red[q];
+  return base + incl - v;
+}
+
+// ---- symbol access -------------------------------------------------------------------------
+
+template <int K>
+__device__ __forceinline__ uint64_t load_elem(const uint8_t* p) {
+  uint64_t u = 0;
+#pragma unroll
+  for (int b = 0; b < K; ++b) u |= uint64_t(p[b]) << (8 * b);
+  return u;
+}
+
+template <int K, bool REORDER>
+__device__ __forceinline__ uint64_t reorder_elem(uint64_t u) {
+  if constexpr (REORDER) {
+    constexpr int W = 8 * K;
+    uint64_t exp = (u >> (W - 9)) & 0xFF, sign = u >> (W - 1), mant = u & ((uint64_t(1) << (W - 9)) - 1);
+    return (exp << (W - 8)) | (sign << (W - 9)) | mant;
+  }
+  return u;
+}
+
+// The 16 symbols of plane b for elements e0 .. e0 + 15 of a chunk (nact of them valid).
+// mode: 2 = 16-byte loads, 1 = 8-byte loads, 0 = bytes.
+template <int K, bool REORDER>
+__device__ __forceinline__ void plane_symbols(const uint8_t* xc, int64_t e0, int nact, int b, int mode, uint32_t* sym) {
+  if (nact == 16 && mode) {
+    uint32_t e[4 * K];
+    load_words(xc + e0 * K, e, 4 * K, mode == 2);
+    reorder_words<K, REORDER, true>(e, 4 * K);
+    uint32_t p[K][4];
+    elements_to_planes<K>(e, p);
+#pragma unroll
+    for (int q = 0; q < K; ++q)
+      if (q == b) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sym[i] = p[q][i];
+      }
+    return;
+  }
+  uint64_t lo = 0, hi = 0;  // two 64-bit accumulators keep the runtime-indexed bytes in registers
+  for (int i = 0; i < nact; ++i) {
+    const uint64_t u = reorder_elem<K, REORDER>(load_elem<K>(xc + (e0 + i) * K));
+    const uint64_t byte = (u >> (8 * b)) & 0xFF;
+    if (i < 8) lo |= byte << (8 * i);
+    else hi |= byte << (8 * (i - 8));
+  }
+  sym[0] = uint32_t(lo);
+  sym[1] = uint32_t(lo >> 32);
+  sym[2] = uint32_t(hi);
+  sym[3] = uint32_t(hi >> 32);
+}
+
+// Histogram all planes over the chunk's whole VB-byte vectors; returns the elements covered.
+// Each thread keeps kHistDepth independent vector loads in flight before its atomics.
+constexpr int kHistDepth = 4;
+
+template <int K, bool REORDER, int VB>
+__device__ __forceinline__ int64_t hist_vectors(const uint8_t* xc, int64_t m, uint32_t* hist, int col) {
+  const int64_t nvec = m * K / VB;
+  for (int64_t v0 = threadIdx.x; v0 < nvec; v0 += kHistDepth * int64_t(blockDim.x)) {
+    uint32_t w[kHistDepth][VB / 4];
+#pragma unroll
+    for (int d = 0; d < kHistDepth; ++d) {
+      const int64_t v = v0 + d * int64_t(blockDim.x);
+      if (v < nvec) load_words(xc + v * VB, w[d], VB / 4, VB == 16);
+    }
+#pragma unroll
+    for (int d = 0; d < kHistDepth; ++d) {
+      if (v0 + d * int64_t(blockDim.x) >= nvec) break;
+      reorder_words<K, REORDER, true>(w[d], VB / 4);
+#pragma unroll
+      for (int q = 0; q < VB; ++q) {
+        const uint32_t byte = (w[d][q >> 2] >> (8 * (q & 3))) & 0xFF;
+        atomicAdd(&hist[(((q % K) << 8) | byte) * kCols + col], 1u);
+      }
+    }
+  }
+  return nvec * VB / K;
+}
+
+// Part `blockIdx.y` of chunk `blockIdx.x`: histograms of all K planes of its elements, written as
+// one partial histogram per plane (no global atomics; the encoder sums the parts).
+template <int K, bool REORDER>
+__global__ void __launch_bounds__(kHistThreads) hist_kernel(EncArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem_raw);  // [K][256][kCols]
+  const int64_t j = blockIdx.x;
+  const int part = blockIdx.y, tid = threadIdx.x;
+  const uint8_t* xc;
+  int64_t m;
+  if (a.in_ptrs) {
+    xc = reinterpret_cast<const uint8_t*>(a.in_ptrs[j]);
+    m = a.in_bytes[j];
+  } else {
+    xc = a.x + j * a.C * K;
+    m = min(a.C, a.n - j * a.C);
+  }
+  m = max(int64_t(0), min(m, a.C));
+  const int64_t per = cdiv(cdiv(m, kHistParts), 16) * 16;
+  const int64_t e0 = min(m, part * per), e1 = min(m, e0 + per);
+  const uint8_t* xs = xc + e0 * K;
+  const int64_t ms = e1 - e0;
+  for (int i = tid; i < K * 256 * kCols; i += kHistThreads) hist[i] = 0;
+  __syncthreads();
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(xs);
+  const int mode = (xa & 15) == 0 ? 2 : (xa & 7) == 0 ? 1 : 0;
+  const int col = tid & (kCols - 1);
+  int64_t done = 0;
+  if (mode == 2) done = hist_vectors<K, REORDER, 16>(xs, ms, hist, col);
+  else if (mode == 1) done = hist_vectors<K, REORDER, 8>(xs, ms, hist, col);
+  for (int64_t e = done + tid; e < ms; e += kHistThreads) {
+    const uint64_t u = reorder_elem<K, REORDER>(load_elem<K>(xs + e * K));
+#pragma unroll
+    for (int b = 0; b < K; ++b) atomicAdd(&hist[((b << 8) | uint32_t((u >> (8 * b)) & 0xFF)) * kCols + col], 1u);
+  }
+  __syncthreads();
+  uint32_t* outp = const_cast<uint32_t*>(a.part_hist) + (j * kHistParts + part) * K * 256;
+  for (int i = tid; i < K * 256; i += kHistThreads) {
+    uint32_t c = 0;
+#pragma unroll
+    for (int q = 0; q < kCols; ++q) c += hist[i * kCols + ((q + i) & (kCols - 1))];
+    outp[i] = c;
+  }
+}
+
+// One encode step of one state for symbol byte I (last symbol first; the decoder runs forward).
+// A state that would leave [L, 2^32) after coding emits its low 16 bits into its own stream,
+// which grows down from the end of the state's slot; the word goes to the lane's 32-halfword
+// staging ring in shared memory (one predicated 2-byte store, no branch).
+template <bool FULL, int I>
+__device__ __forceinline__ void encode_step(uint32_t& x, uint32_t& wp, uint16_t* stage, const uint32_t* sym,
+                                            const uint4* tab, bool act) {
+  const uint4 e = tab[get_byte(sym, I)];  // {magic, bias, (M - f) | shift << 16, f}
+  const bool emit = (FULL || act) && (x >> 20) >= e.w;
+  wp -= emit;
+  if (emit) stage[wp & 31] = uint16_t(x);
+  x = emit ? x >> 16 : x;
+  const uint32_t tq = __umulhi(x, e.x);
+  const uint32_t q = (tq + ((x - tq) >> 1)) >> (e.z >> 16);
+  const uint32_t xn = x + e.y + q * (e.z & 0xFFFFu);
+  x = (FULL || act) ? xn : x;
+}
+
+// 16 steps of the lane's kEncChains states, interleaved so the independent chains overlap.
+template <bool FULL>
+__device__ __forceinline__ void encode_round(uint32_t* x, uint32_t* wp, uint16_t* const* stage,
+                                             const uint32_t (*sym)[4], const uint4* tab, const int* nact) {
+#define ZN_ESTEP(I)                                                                                   \
+  _Pragma("unroll") for (int c = 0; c < kEncChains; ++c)                                              \
+      encode_step<FULL, I>(x[c], wp[c], stage[c], sym[c], tab, (I) < nact[c]);
+  ZN_ESTEP(15) ZN_ESTEP(14) ZN_ESTEP(13) ZN_ESTEP(12) ZN_ESTEP(11) ZN_ESTEP(10) ZN_ESTEP(9) ZN_ESTEP(8)
+  ZN_ESTEP(7) ZN_ESTEP(6) ZN_ESTEP(5) ZN_ESTEP(4) ZN_ESTEP(3) ZN_ESTEP(2) ZN_ESTEP(1) ZN_ESTEP(0)
+#undef ZN_ESTEP
+}
+
+// ---- the encoder ----------------------------------------------------------------------------
+
+template <int K, bool REORDER>
+__global__ void __launch_bounds__(kEncThreads) encode_kernel(EncArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint4* etab = reinterpret_cast<uint4*>(smem_raw);                         // [K][256]
+  EncSmem& S = *reinterpret_cast<EncSmem*>(smem_raw + K * 256 * 16);
+
+  const int64_t j = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint8_t* xc;
+  int64_t m;
+  if (a.in_ptrs) {
+    xc = reinterpret_cast<const uint8_t*>(a.in_ptrs[j]);
+    m = a.in_bytes[j];
+  } else {
+    xc = a.x + j * a.C * K;
+    m = min(a.C, a.n - j * a.C);
+  }
+  if (m <= 0 || m > a.C) {
+    if (tid < K) a.comp_bytes[tid * a.nch + j] = -1;
+    return;
+  }
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(xc);
+  const int mode = (xa & 15) == 0 ? 2 : (xa & 7) == 0 ? 1 : 0;
+
+  const Geom g = geom_of(m, a.t);
+  const int64_t thr = a.allow_skip ? int64_t(double(m) * a.threshold) : INT64_MAX;
+
+  // Phase B: per plane, frequencies, skip decision, coder table and payload header.  Thread t owns
+  // symbols kEncSym * t .. kEncSym * t + kEncSym - 1.
+  for (int b = 0; b < K; ++b) {
+    const uint64_t u = uint64_t(b) * a.nch + j;
+    uint8_t* meta = a.meta + u * a.meta_slot;
+    uint32_t cc[kEncSym], ff[kEncSym];
+    // Phase A: the plane's histogram is the sum of the parts' (hist_kernel).
+    uint32_t npres = 0;
+#pragma unroll
+    for (int h = 0; h < kEncSym; ++h) {
+      const int s = kEncSym * tid + h;
+      uint32_t c = 0;
+#pragma unroll
+      for (int q = 0; q < kHistParts; ++q) c += a.part_hist[((j * kHistParts + q) * K + b) * 256 + s];
+      cc[h] = c;
+      npres += c > 0;
+    }
+    const uint32_t np = block_sum_u(npres, S.red_u);
+    unsigned long long key = 0;
+#pragma unroll
+    for (int h = 0; h < kEncSym; ++h)
+      if (cc[h]) {
+        unsigned long long k2 = (static_cast<unsigned long long>(cc[h]) << 32) | uint32_t(255 - (kEncSym * tid + h));
+        key = k2 > key ? k2 : key;
+      }
+    const int smax = 255 - int(block_max_ull(key, S.red_ull) & 0xFFFFFFFFu);
+    // orc_normalize (oracle/zn_oracle.c) on the GPU.
+#pragma unroll
+    for (int h = 0; h < kEncSym; ++h) {
+      const uint64_t q = (uint64_t(cc[h]) * kM + uint64_t(m / 2)) / uint64_t(m);
+      ff[h] = cc[h] ? (q < 1 ? 1u : uint32_t(q)) : 0u;
+    }
+    if (np == 1) {
+#pragma unroll
+      for (int h = 0; h < kEncSym; ++h) ff[h] = (kEncSym * tid + h == smax) ? kM : 0u;
+    } else {
+      uint32_t fs = 0;
+#pragma unroll
+      for (int h = 0; h < kEncSym; ++h) fs += ff[h];
+      const int64_t d = int64_t(kM) - int64_t(block_sum_u(fs, S.red_u));
+      __syncthreads();
+#pragma unroll
+      for (int h = 0; h < kEncSym; ++h)
+        if (kEncSym * tid + h == smax) S.f[0] = ff[h];
+      __syncthreads();
+      const int64_t fmax = S.f[0];
+      if (fmax + d >= 1) {
+#pragma unroll
+        for (int h = 0; h < kEncSym; ++h)
+          if (kEncSym * tid + h == smax) ff[h] = uint32_t(fmax + d);
+      } else {
+        fs = 0;
+#pragma unroll
+        for (int h = 0; h < kEncSym; ++h) {
+          ff[h] = cc[h] ? 1u + uint32_t((uint64_t(cc[h]) * uint64_t(kM - np)) / uint64_t(m)) : 0u;
+          fs += ff[h];
+        }
+        const int64_t sum2 = block_sum_u(fs, S.red_u);
+#pragma unroll
+        for (int h = 0; h < kEncSym; ++h)
+          if (kEncSym * tid + h == smax) ff[h] += uint32_t(int64_t(kM) - sum2);
+      }
+    }
+    // Cumulative frequencies and ranks of present symbols.
+    uint32_t fsum = 0, psum = 0;
+#pragma unroll
+    for (int h = 0; h < kEncSym; ++h) {
+      fsum += ff[h];
+      psum += ff[h] > 0;
+    }
+    uint32_t cum = block_excl_scan(fsum, S.red_u);
+    uint32_t rank = block_excl_scan(psum, S.red_u);
+    // Entropy lower bound of the payload; skip planes that cannot beat the passthrough budget.
+    float bits = 0.f;
+#pragma unroll
+    for (int h = 0; h < kEncSym; ++h)
+      if (cc[h]) {
+        const float fr = float(ff[h]);
+        bits += float(cc[h]) * (float(kScaleBits) - log2f(fr) + log2f(1.f - fr * (1.f / 65536.f)));
+      }
+    const float info = block_sum_f(bits, S.red_f);
+    const int64_t mb = meta_bytes(int(np), g);
+    const float states = float(g.nu) * kLanes;
+    const float lb = 2.f * (info - 16.f * states) / 16.1f + float(mb) - 64.f - float(m) * (1.f / 1024.f);
+    const bool skip = lb >= float(thr);
+    if (tid == 0) {
+      S.skip[b] = skip;
+      S.npl[b] = int(np);
+    }
+    if (skip) {
+      if (tid == 0) a.comp_bytes[u] = -1;
+      __syncthreads();
+      continue;
+    }
+    // Encoder table: x' = x + bias + q * (M - f), q = floor(x / f) by multiply-high
+    // (Granlund and Montgomery, "Division by invariant integers using multiplication", 1994).
+    for (int i = tid; i < 96; i += kEncThreads) S.fbuf[i] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < kEncSym; ++h) {
+      const int s = kEncSym * tid + h;
+      const uint32_t f = ff[h];
+      uint4 e = make_uint4(0, 0, 0, 0);
+      if (f == 1) {
+        e = make_uint4(0xFFFFFFFFu, cum + kM - 1, (kM - 1) | (0u << 16), 1u);
+      } else if (f > 1) {
+        const int l = 32 - __clz(f - 1);
+        const uint32_t mg = uint32_t(((uint64_t((uint64_t(1) << l) - f) << 32) / f) + 1);
+        e = make_uint4(mg, cum, (kM - f) | (uint32_t(l - 1) << 16), f);
+      }
+      etab[b * 256 + s] = e;
+      cum += f;
+      // Payload header field: f - 1 as 12 bits at field index rank.
+      if (f) {
+        const uint32_t pos = 12 * rank++, v = f - 1;
+        atomicOr(&S.fbuf[pos >> 5], v << (pos & 31));
+        if ((pos & 31) > 20) atomicOr(&S.fbuf[(pos >> 5) + 1], v >> (32 - (pos & 31)));
+      }
+    }
+    // Presence bitmap: symbol s = kEncSym * t + h is bit s; warp w covers symbols
+    // 32 kEncSym w .. 32 kEncSym (w + 1) - 1, and its ballot h holds bit kEncSym * lane + h of them.
+    uint32_t bm[kEncSym];
+#pragma unroll
+    for (int h = 0; h < kEncSym; ++h) bm[h] = __ballot_sync(0xFFFFFFFFu, ff[h] > 0);
+    __syncthreads();
+    if (lane < 4 * kEncSym) {  // this warp's bitmap byte `lane`: its symbols 8 lane .. 8 lane + 7
+      uint32_t byte = 0;
+#pragma unroll
+      for (int bit = 0; bit < 8; ++bit) {
+        const int k = 8 * lane + bit;
+        byte |= ((bm[k % kEncSym] >> (k / kEncSym)) & 1u) << bit;
+      }
+      meta[2 + 4 * kEncSym * warp + lane] = uint8_t(byte);
+    }
+    const int64_t tb = table_bytes(int(np));
+    for (int64_t i = tid; i < tb - 34; i += kEncThreads)
+      meta[34 + i] = i < 384 ? uint8_t(S.fbuf[i >> 2] >> (8 * (i & 3))) : 0;
+    if (tid == 0) {
+      meta[0] = uint8_t(a.t);
+      meta[1] = 0;
+    }
+    __syncthreads();
+  }
+  __syncthreads();
+
+  // Phase C: encode.  A warp item is (plane, group of 8 sub-chunks); lane l of 8-lane segment g
+  // runs chain c on sub-chunk 8 * group + 4 * c + g, each chain one state with its own stream slot.
+  const int ngroups = int(cdiv(g.nu, 4 * kEncChains));
+  int nplanes = 0;
+  for (int b = 0; b < K; ++b) nplanes += !S.skip[b];
+  if (tid < K) S.nwsum[tid] = 0;
+  __syncthreads();
+  const int seg = lane >> 3, l = lane & 7;
+  const int rounds = int(g.sc / kRound);
+  for (int item = warp; item < nplanes * ngroups; item += kEncThreads / 32) {
+    int b = 0, seen = 0;
+    for (int q = 0; q < K; ++q)
+      if (!S.skip[q]) {
+        if (seen == item / ngroups) b = q;
+        ++seen;
+      }
+    const uint64_t u = uint64_t(b) * a.nch + j;
+    const uint4* tab = etab + b * 256;
+    int gi[kEncChains];
+    bool valid[kEncChains];
+    int64_t base[kEncChains], len[kEncChains];
+    uint16_t* out[kEncChains];
+    uint16_t* stage[kEncChains];
+    uint32_t x[kEncChains], wp[kEncChains], flushed[kEncChains];
+    uint32_t nxt[kEncChains][4 * K];
+#pragma unroll
+    for (int c = 0; c < kEncChains; ++c) {
+      gi[c] = 4 * kEncChains * (item % ngroups) + 4 * c + seg;
+      valid[c] = gi[c] < g.nu;
+      base[c] = int64_t(gi[c]) * g.sc;
+      len[c] = valid[c] ? min(g.sc, m - base[c]) : 0;
+      out[c] = a.streams + u * a.unit_words + int64_t(gi[c]) * a.sub_words + int64_t(l) * a.lane_words;
+      x[c] = kL;
+      wp[c] = flushed[c] = uint32_t(a.lane_words);  // the stream grows down from the slot's end
+      stage[c] = reinterpret_cast<uint16_t*>(S.stage[tid]);  // one ring per lane: kEncChains == 1
+    }
+    // The elements of the next (lower) round are loaded while the current round is encoded.
+    auto full_round = [&](int c, int r) {
+      return mode != 0 && len[c] - (int64_t(r) * kRound + l * kSteps) >= kSteps;
+    };
+#pragma unroll
+    for (int c = 0; c < kEncChains; ++c)
+      if (rounds > 0 && full_round(c, rounds - 1))
+        load_words(xc + (base[c] + int64_t(rounds - 1) * kRound + l * kSteps) * K, nxt[c], 4 * K, mode == 2);
+    for (int r = rounds - 1; r >= 0; --r) {
+      uint32_t sym[kEncChains][4];
+      int nact[kEncChains];
+#pragma unroll
+      for (int c = 0; c < kEncChains; ++c) {
+        const int64_t off = int64_t(r) * kRound + l * kSteps;
+        nact[c] = int(max(int64_t(0), min(int64_t(kSteps), len[c] - off)));
+        if (full_round(c, r)) {
+          reorder_words<K, REORDER, true>(nxt[c], 4 * K);
+          uint32_t pl[K][4];
+          elements_to_planes<K>(nxt[c], pl);
+#pragma unroll
+          for (int q = 0; q < K; ++q)
+            if (q == b) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) sym[c][i] = pl[q][i];
+            }
+        } else {
+          plane_symbols<K, REORDER>(xc, base[c] + off, nact[c], b, 0, sym[c]);
+        }
+        if (r > 0 && full_round(c, r - 1))
+          load_words(xc + (base[c] + int64_t(r - 1) * kRound + l * kSteps) * K, nxt[c], 4 * K, mode == 2);
+      }
+      if (nact[0] == kSteps && nact[kEncChains - 1] == kSteps) encode_round<true>(x, wp, stage, sym, tab, nact);
+      else encode_round<false>(x, wp, stage, sym, tab, nact);
+      // Completed 16-byte blocks of the staging ring go to the stream slot.
+#pragma unroll
+      for (int c = 0; c < kEncChains; ++c)
+        while (flushed[c] - wp[c] >= 8) {
+          flushed[c] -= 8;
+          *reinterpret_cast<uint4*>(out[c] + flushed[c]) = S.stage[tid][(flushed[c] / 8) & 3];
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < kEncChains; ++c)
+      for (uint32_t h = wp[c]; h < flushed[c]; ++h) out[c][h] = stage[c][h & 31];
+#pragma unroll
+    for (int c = 0; c < kEncChains; ++c) {
+      if (!valid[c]) continue;
+      uint8_t* meta = a.meta + u * a.meta_slot;
+      const uint32_t nwords = uint32_t(a.lane_words) - wp[c];
+      const int64_t tb = table_bytes(S.npl[b]);
+      const int64_t fi = int64_t(gi[c]) * kLanes + l;
+      *reinterpret_cast<uint32_t*>(meta + tb + lengths_bytes(g) + 4 * fi) = x[c];
+      if (g.lw == 2) *reinterpret_cast<uint16_t*>(meta + tb + 2 * fi) = uint16_t(nwords);
+      else *reinterpret_cast<uint32_t*>(meta + tb + 4 * fi) = nwords;
+      atomicAdd(&S.nwsum[b], int(nwords));
+    }
+  }
+  __syncthreads();
+  // Zero the pad of the length field area and publish the payload sizes.
+  if (tid < K && !S.skip[tid]) {
+    const int b = tid;
+    const uint64_t u = uint64_t(b) * a.nch + j;
+    uint8_t* meta = a.meta + u * a.meta_slot;
+    const int npres = S.npl[b];
+    const int64_t tb = table_bytes(npres);
+    for (int64_t i = int64_t(g.nu) * kLanes * g.lw; i < lengths_bytes(g); ++i) meta[tb + i] = 0;
+    a.comp_bytes[u] = int32_t(meta_bytes(npres, g) + 2 * int64_t(S.nwsum[b]));
+  }
+}
+
+// ---- scan: passthrough rule, tables, destinations (src/cuzipnn/_codec.py:361-403) ------------
+
+constexpr int kScanThreads = 1024;
+constexpr int kScanPer = 4;
+
+struct HeaderParam {
+  uint8_t bytes[24 + 8 * 64];
+  int len;
+};
+
+struct ScanArgs {
+  const int32_t* comp_bytes;
+  int64_t total, nch, C, n;
+  double threshold;
+  int64_t sizes_off, idx_off;
+  uint8_t* out;
+  int64_t* dst_rel;      // per unit: offset from data_off, with bit 62 set if coded
+  int64_t* scalars;      // [0] = data_off, [1] = size
+  uint64_t* size_out;
+  HeaderParam header;
+};
+
+__device__ __forceinline__ void block_scan2(int64_t& a, int64_t& b, int64_t& ta, int64_t& tb, int64_t* sm) {
+  // Exclusive scan of (a, b) over kScanThreads threads; totals returned in ta, tb.
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int64_t ia = a, ib = b;
+  for (int o = 1; o < 32; o <<= 1) {
+    int64_t ua = __shfl_up_sync(0xFFFFFFFFu, ia, o), ub = __shfl_up_sync(0xFFFFFFFFu, ib, o);
+    if (lane >= o) { ia += ua; ib += ub; }
+  }
+  if (lane == 31) { sm[w] = ia; sm[32 + w] = ib; }
+  __syncthreads();
+  if (w == 0) {
+    int64_t va = sm[lane], vb = sm[32 + lane];
+    for (int o = 1; o < 32; o <<= 1) {
+      int64_t ua = __shfl_up_sync(0xFFFFFFFFu, va, o), ub = __shfl_up_sync(0xFFFFFFFFu, vb, o);
+      if (lane >= o) { va += ua; vb += ub; }
+    }
+    sm[64 + lane] = va;
+    sm[96 + lane] = vb;
+  }
+  __syncthreads();
+  const int64_t pa = w ? sm[64 + w - 1] : 0, pb = w ? sm[96 + w - 1] : 0;
+  ta = sm[64 + 31];
+  tb = sm[96 + 31];
+  a = pa + ia - a;
+  b = pb + ib - b;
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
+  __shared__ int64_t sm[128];
+  const int tid = threadIdx.x;
+  const int64_t last = a.n - (a.nch - 1) * a.C;
+  int64_t carry_data = 0, carry_comp = 0;
+  for (int64_t start = 0; start < a.total; start += int64_t(kScanThreads) * kScanPer) {
+    int64_t stored[kScanPer];
+    bool use[kScanPer];
+    int64_t sd = 0, sc = 0;
+#pragma unroll
+    for (int q = 0; q < kScanPer; ++q) {
+      const int64_t i = start + int64_t(tid) * kScanPer + q;
+      use[q] = false;
+      stored[q] = 0;
+      if (i < a.total) {
+        const int64_t jj = i % a.nch;
+        const int64_t raw = jj == a.nch - 1 ? last : a.C;
+        const int64_t thr = __double2ll_rz(double(raw) * a.threshold);
+        const int64_t c = a.comp_bytes[i];
+        use[q] = c >= 0 && c < thr;
+        stored[q] = use[q] ? c : raw;
+        *reinterpret_cast<int32_t*>(a.out + a.sizes_off + 4 * i) = int32_t(stored[q]);
+        sd += align8(stored[q]);
+        sc += use[q];
+      }
+    }
+    int64_t td, tc;
+    block_scan2(sd, sc, td, tc, sm);
+#pragma unroll
+    for (int q = 0; q < kScanPer; ++q) {
+      const int64_t i = start + int64_t(tid) * kScanPer + q;
+      if (i < a.total) {
+        a.dst_rel[i] = (carry_data + sd) | (int64_t(use[q]) << 62);
+        if (use[q]) *reinterpret_cast<int32_t*>(a.out + a.idx_off + 4 * (carry_comp + sc)) = int32_t(i);
+        sd += align8(stored[q]);
+        sc += use[q];
+      }
+    }
+    carry_data += td;
+    carry_comp += tc;
+  }
+  const int64_t n_comp = carry_comp;
+  const int64_t data_off = align8(a.idx_off + 4 * n_comp);
+  const int64_t size = data_off + carry_data;
+  for (int i = tid; i < a.header.len; i += kScanThreads) {
+    uint8_t v = a.header.bytes[i];
+    if (i >= 12 && i < 16) v = uint8_t(uint64_t(n_comp) >> (8 * (i - 12)));
+    a.out[i] = v;
+  }
+  for (int64_t i = a.idx_off + 4 * n_comp + tid; i < data_off; i += kScanThreads) a.out[i] = 0;
+  if (tid == 0) {
+    a.scalars[0] = data_off;
+    a.scalars[1] = size;
+    *a.size_out = uint64_t(size);
+  }
+}
+
+// ---- pack (src/cuzipnn/_codec.py:381-403) ---------------------------------------------------
+
+constexpr int kPackThreads = 256;
+
+struct PackArgs {
+  const uint8_t* x;
+  int64_t n, C, nch;
+  const int32_t* comp_bytes;
+  const int64_t* dst_rel;
+  const int64_t* scalars;
+  const uint8_t* meta;
+  int64_t meta_slot;
+  const uint16_t* streams;
+  int64_t unit_words, sub_words, lane_words;
+  int t;
+  uint8_t* out;
+};
+
+__device__ __forceinline__ int count_present(const uint8_t* meta) {
+  int np = 0;
+  for (int q = 0; q < 32; ++q) np += __popc(uint32_t(meta[2 + q]));
+  return np;
+}
+
+// Copy halfwords [h0, h1) of one coded payload (the meta block, then the sub-chunk streams from
+// the tails of their scratch slots) to dst, which is 2-byte aligned.  Threads of the CTA stride
+// over the range with kCopyDepth loads in flight.
+constexpr int kCopyDepth = 4;
+
+__device__ __forceinline__ void copy_halfwords(uint16_t* dst, const uint16_t* src, int64_t n) {
+  for (int64_t i0 = threadIdx.x; i0 < n; i0 += kCopyDepth * int64_t(blockDim.x)) {
+    uint16_t v[kCopyDepth];
+#pragma unroll
+    for (int d = 0; d < kCopyDepth; ++d) {
+      const int64_t i = i0 + d * int64_t(blockDim.x);
+      if (i < n) v[d] = src[i];
+    }
+#pragma unroll
+    for (int d = 0; d < kCopyDepth; ++d) {
+      const int64_t i = i0 + d * int64_t(blockDim.x);
+      if (i < n) dst[i] = v[d];
+    }
+  }
+}
+
+// Exclusive prefix sums of the nu * 8 stream lengths of a payload into pre[] (shared), by all
+// kPackThreads threads (two lengths per thread, up to 512).
+__device__ void stream_prefix(const uint8_t* meta, int64_t tb, const Geom& g, int32_t* pre, int32_t* warp_tot) {
+  const int S = g.nu * kLanes, t = threadIdx.x, lane = t & 31, w = t >> 5;
+  int32_t v[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int fi = 2 * t + h;
+    v[h] = fi >= S ? 0
+           : g.lw == 2 ? int32_t(reinterpret_cast<const uint16_t*>(meta + tb)[fi])
+                       : int32_t(reinterpret_cast<const uint32_t*>(meta + tb)[fi]);
+  }
+  int32_t incl = v[0] + v[1];
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t x = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += x;
+  }
+  __syncthreads();
+  if (lane == 31) warp_tot[w] = incl;
+  __syncthreads();
+  int32_t base = 0;
+  for (int q = 0; q < w; ++q) base += warp_tot[q];
+  const int32_t ex = base + incl - v[0] - v[1];
+  pre[2 * t] = ex;
+  pre[2 * t + 1] = ex + v[0];
+  __syncthreads();
+}
+
+// Copy part `part` of `nparts` of one coded payload to dst (2-byte aligned): the meta block (part
+// 0), then its share of the nu * 8 streams, each from the tail of its slot, one warp per stream.
+// Called by all threads of the CTA.
+__device__ void copy_payload(const PackArgs& a, uint64_t u, int64_t m, uint8_t* dst, int npres, int part, int nparts,
+                             int32_t* pre, int32_t* warp_tot) {
+  const uint8_t* meta = a.meta + u * a.meta_slot;
+  const Geom g = geom_of(m, a.t);
+  const int64_t tb = table_bytes(npres);
+  const int64_t mh = meta_bytes(npres, g) / 2;
+  uint16_t* d16 = reinterpret_cast<uint16_t*>(dst);
+  if (part == 0) copy_halfwords(d16, reinterpret_cast<const uint16_t*>(meta), mh);
+  stream_prefix(meta, tb, g, pre, warp_tot);
+  const int S = g.nu * kLanes;
+  const int f0 = int(int64_t(S) * part / nparts), f1 = int(int64_t(S) * (part + 1) / nparts);
+  const int lane = threadIdx.x & 31, nwarps = blockDim.x / 32;
+  for (int fi = f0 + int(threadIdx.x >> 5); fi < f1; fi += nwarps) {
+    const int gi = fi / kLanes, l = fi % kLanes;
+    const int32_t n = fi + 1 < S ? pre[fi + 1] - pre[fi]
+                      : (g.lw == 2 ? int32_t(reinterpret_cast<const uint16_t*>(meta + tb)[fi])
+                                   : int32_t(reinterpret_cast<const uint32_t*>(meta + tb)[fi]));
+    const uint16_t* src = a.streams + u * a.unit_words + int64_t(gi) * a.sub_words + int64_t(l) * a.lane_words +
+                          (a.lane_words - n);
+    uint16_t* d = d16 + mh + pre[fi];
+    for (int i = lane; i < n; i += 32) d[i] = src[i];
+  }
+  __syncthreads();
+}
+
+// Grid (chunk, part): part p of chunk j handles 1/kPackParts of every coded payload and of the
+// chunk's elements for the raw planes.  Chunks run in reverse order, so the most recently encoded
+// (and read) chunks are still in L2.
+constexpr int kPackParts = 8;
+
+template <int K, bool REORDER>
+__global__ void __launch_bounds__(kPackThreads) pack_kernel(PackArgs a) {
+  __shared__ int32_t pre[512];
+  __shared__ int32_t warp_tot[kPackThreads / 32];
+  const int64_t j = a.nch - 1 - blockIdx.x;
+  const int part = blockIdx.y;
+  const int64_t m = min(a.C, a.n - j * a.C);
+  const int64_t data_off = a.scalars[0];
+  __shared__ int npres[K];
+  uint8_t* dst[K];
+  bool coded[K];
+  bool any_raw = false;
+  if (threadIdx.x < K) {
+    const uint64_t u = uint64_t(threadIdx.x) * a.nch + j;
+    npres[threadIdx.x] = (a.dst_rel[u] >> 62) & 1 ? count_present(a.meta + u * a.meta_slot) : 0;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int b = 0; b < K; ++b) {
+    const uint64_t u = uint64_t(b) * a.nch + j;
+    const int64_t d = a.dst_rel[u];
+    coded[b] = (d >> 62) & 1;
+    dst[b] = a.out + data_off + (d & ((int64_t(1) << 62) - 1));
+    any_raw |= !coded[b];
+    if (coded[b]) {
+      const int64_t size = a.comp_bytes[u];
+      copy_payload(a, u, m, dst[b], npres[b], part, kPackParts, pre, warp_tot);
+      if (part == kPackParts - 1 && threadIdx.x < 8 && size + threadIdx.x < align8(size)) dst[b][size + threadIdx.x] = 0;
+    }
+  }
+  if (!any_raw) return;
+  const uint8_t* xc = a.x + j * a.C * K;
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(xc);
+  const int mode = (xa & 15) == 0 ? 2 : (xa & 7) == 0 ? 1 : 0;
+  const int64_t ngrp = mode ? m / 16 : 0;
+  const int64_t gper = cdiv(ngrp, kPackParts);
+  const int64_t g0 = part * gper, g1 = min(ngrp, g0 + gper);
+  for (int64_t v0 = g0 + threadIdx.x; v0 < g1; v0 += 2 * kPackThreads) {
+    uint32_t e[2][4 * K];
+#pragma unroll
+    for (int d = 0; d < 2; ++d) {
+      const int64_t v = v0 + d * kPackThreads;
+      if (v < g1) load_words(xc + v * 16 * K, e[d], 4 * K, mode == 2);
+    }
+#pragma unroll
+    for (int d = 0; d < 2; ++d) {
+      const int64_t v = v0 + d * kPackThreads;
+      if (v >= g1) break;
+      reorder_words<K, REORDER, true>(e[d], 4 * K);
+      uint32_t p[K][4];
+      elements_to_planes<K>(e[d], p);
+#pragma unroll
+      for (int b = 0; b < K; ++b)
+        if (!coded[b]) {
+          uint8_t* q = dst[b] + v * 16;
+          if ((reinterpret_cast<uintptr_t>(q) & 15) == 0) *reinterpret_cast<uint4*>(q) = make_uint4(p[b][0], p[b][1], p[b][2], p[b][3]);
+          else {
+            reinterpret_cast<uint2*>(q)[0] = make_uint2(p[b][0], p[b][1]);
+            reinterpret_cast<uint2*>(q)[1] = make_uint2(p[b][2], p[b][3]);
+          }
+        }
+    }
+  }
+  if (part != kPackParts - 1) return;
+  for (int64_t e = ngrp * 16 + threadIdx.x; e < m; e += kPackThreads) {
+    const uint64_t w = reorder_elem<K, REORDER>(load_elem<K>(xc + e * K));
+#pragma unroll
+    for (int b = 0; b < K; ++b)
+      if (!coded[b]) dst[b][e] = uint8_t(w >> (8 * b));
+  }
+  if (threadIdx.x < 8 && m + threadIdx.x < align8(m)) {
+#pragma unroll
+    for (int b = 0; b < K; ++b)
+      if (!coded[b]) dst[b][m + threadIdx.x] = 0;
+  }
+}
+
+// ---- batched seam: assemble each payload into the caller's out_ptrs[i] ---------------------
+
+__global__ void __launch_bounds__(kPackThreads) assemble_kernel(PackArgs a, const int64_t* in_bytes,
+                                                                const int64_t* out_ptrs, int64_t* out_bytes,
+                                                                int32_t* statuses) {
+  const int64_t i = blockIdx.x;
+  const int64_t size = a.comp_bytes[i];
+  if (size < 0) {
+    if (threadIdx.x == 0) { out_bytes[i] = 0; statuses[i] = 1; }
+    return;
+  }
+  __shared__ int npres;
+  __shared__ int32_t pre[512];
+  __shared__ int32_t warp_tot[kPackThreads / 32];
+  if (threadIdx.x == 0) npres = count_present(a.meta + uint64_t(i) * a.meta_slot);
+  __syncthreads();
+  copy_payload(a, uint64_t(i), in_bytes[i], reinterpret_cast<uint8_t*>(out_ptrs[i]), npres, 0, 1, pre, warp_tot);
+  if (threadIdx.x == 0) { out_bytes[i] = size; statuses[i] = 0; }
+}
+
+// ---- host-side launch helpers ---------------------------------------------------------------
+
+struct EncLayout {
+  int64_t meta_slot, unit_words, sub_words, lane_words;
+  size_t off_comp, off_dst, off_scalars, off_hist, off_meta, off_streams, total;
+};
+
+EncLayout enc_layout(int64_t units, int64_t C, int t) {
+  EncLayout L;
+  // A shorter last unit can have more (smaller) sub-chunks than a full one, so the slots are
+  // sized for 2^t sub-chunks of the full unit's sub-chunk length.
+  const Geom g = geom_of(C, t);
+  L.meta_slot = (max_meta_bytes(t) + 15) & ~int64_t(15);
+  L.lane_words = ((g.sc / kLanes) + 7) & ~int64_t(7);  // multiple of 8 words: 16-byte aligned slots
+  L.sub_words = kLanes * L.lane_words;
+  L.unit_words = L.sub_words << t;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t r = o; o = (o + bytes + 255) & ~size_t(255); return r; };
+  L.off_comp = take(size_t(units) * 4);
+  L.off_dst = take(size_t(units) * 8);
+  L.off_scalars = take(64);
+  L.off_hist = take(size_t(units) * kHistParts * 256 * 4);  // units = K * nch
+  L.off_meta = take(size_t(units) * size_t(L.meta_slot));
+  L.off_streams = take(size_t(units) * size_t(L.unit_words) * 2);
+  L.total = o;
+  return L;
+}
+
+size_t enc_smem(int K) { return size_t(K) * 256 * 16 + sizeof(EncSmem); }
+size_t hist_smem(int K) { return size_t(K) * 256 * kCols * 4; }
+
+template <int K, bool REORDER>
+int launch_encode(const EncArgs& a, int64_t grid, cudaStream_t s) {
+  const size_t hs = hist_smem(K);
+  auto hf = hist_kernel<K, REORDER>;
+  if (int rc = set_max_smem(reinterpret_cast<const void*>(hf), int(hs))) return rc;
+  hf<<<dim3(unsigned(grid), kHistParts), kHistThreads, hs, s>>>(a);
+  const size_t sm = enc_smem(K);
+  auto fn = encode_kernel<K, REORDER>;
+  if (int rc = set_max_smem(reinterpret_cast<const void*>(fn), int(sm))) return rc;
+  fn<<<unsigned(grid), kEncThreads, sm, s>>>(a);
+  count_launch(2);
+  return check_launch("encode_kernel");
+}
+
+template <int K, bool REORDER>
+void launch_pack(const PackArgs& p, int64_t grid, cudaStream_t s) {
+  pack_kernel<K, REORDER><<<dim3(unsigned(grid), kPackParts), kPackThreads, 0, s>>>(p);
+  count_launch();
+}
+
+int sub_log2(int sub_chunks) {
+  for (int t = kMinSubLog2; t <= kMaxSubLog2; ++t)
+    if (sub_chunks == (1 << t)) return t;
+  return -1;
+}
+
+}  // namespace
+}  // namespace zn
+
+using namespace zn;
+
+extern "C" {
+
+int64_t zn_ans_max_compressed_chunk_bytes(int64_t chunk_bytes, int sub_chunks) {
+  const int t = sub_log2(sub_chunks);
+  if (t < 0 || chunk_bytes <= 0 || chunk_bytes > kMaxChunkBytes) return -1;
+  return max_payload(chunk_bytes, t);
+}
+
+size_t zn_ans_compress_temp_bytes(int64_t count, int64_t chunk_bytes, int sub_chunks) {
+  const int t = sub_log2(sub_chunks);
+  if (t < 0 || count < 0 || chunk_bytes <= 0) return 0;
+  return enc_layout(count, chunk_bytes, t).total;
+}
+
+int zn_ans_compress(const int64_t* in_ptrs, const int64_t* in_bytes, int64_t chunk_bytes, int64_t count,
+                    const int64_t* out_ptrs, int64_t* out_bytes, int32_t* statuses, int sub_chunks, void* temp,
+                    size_t temp_bytes, void* stream) {
+  const int t = sub_log2(sub_chunks);
+  if (t < 0 || count < 0 || count > 0x7FFFFFFF || chunk_bytes <= 0 || chunk_bytes > kMaxChunkBytes)
+    return set_error(ZN_ERR_INVALID, "zn_ans_compress: bad arguments");
+  if (count == 0) return ZN_OK;
+  const EncLayout L = enc_layout(count, chunk_bytes, t);
+  if (!temp || temp_bytes < L.total) return set_error(ZN_ERR_SPACE, "zn_ans_compress: temp buffer too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* tb = static_cast<uint8_t*>(temp);
+  EncArgs a{};
+  a.in_ptrs = in_ptrs;
+  a.in_bytes = in_bytes;
+  a.C = chunk_bytes;
+  a.nch = count;
+  a.t = t;
+  a.allow_skip = false;
+  a.threshold = 1.0;
+  a.meta = tb + L.off_meta;
+  a.meta_slot = L.meta_slot;
+  a.streams = reinterpret_cast<uint16_t*>(tb + L.off_streams);
+  a.unit_words = L.unit_words;
+  a.sub_words = L.sub_words;
+  a.lane_words = L.lane_words;
+  a.comp_bytes = reinterpret_cast<int32_t*>(tb + L.off_comp);
+  a.part_hist = reinterpret_cast<uint32_t*>(tb + L.off_hist);
+  if (int rc = launch_encode<1, false>(a, count, s)) return rc;
+  PackArgs p{};
+  p.C = chunk_bytes;
+  p.nch = count;
+  p.comp_bytes = a.comp_bytes;
+  p.meta = a.meta;
+  p.meta_slot = a.meta_slot;
+  p.streams = a.streams;
+  p.unit_words = a.unit_words;
+  p.sub_words = a.sub_words;
+  p.lane_words = a.lane_words;
+  p.t = t;
+  assemble_kernel<<<unsigned(count), kPackThreads, 0, s>>>(p, in_bytes, out_ptrs, out_bytes, statuses);
+  count_launch();
+  return check_launch("zn_ans_compress");
+}
+
+int64_t zn_compress_bound(int64_t n, int k, int ndim, int64_t chunk_bytes) {
+  if (n < 0 || k <= 0 || ndim < 0 || chunk_bytes <= 0) return -1;
+  const int64_t nch = cdiv(n, chunk_bytes), total = int64_t(k) * nch;
+  const int64_t head = align8(24 + 8 * int64_t(ndim) + 8 * total);
+  const int64_t data = nch ? int64_t(k) * ((nch - 1) * align8(chunk_bytes) + align8(n - (nch - 1) * chunk_bytes)) : 0;
+  return head + data;
+}
+
+size_t zn_compress_temp_bytes(int64_t n, int k, int64_t chunk_bytes, int sub_chunks) {
+  const int t = sub_log2(sub_chunks);
+  if (t < 0 || n < 0 || k <= 0 || chunk_bytes <= 0) return 0;
+  return enc_layout(int64_t(k) * cdiv(n, chunk_bytes), chunk_bytes, t).total;
+}
+
+int zn_compress(const void* x, int64_t n, int k, int reorder, const void* header, int header_bytes,
+                int64_t chunk_bytes, int sub_chunks, double threshold, void* out, int64_t out_capacity,
+                uint64_t* size_out, void* temp, size_t temp_bytes, void* stream) {
+  const int t = sub_log2(sub_chunks);
+  if (t < 0 || n < 0 || (k != 1 && k != 2 && k != 4 && k != 8) || (reorder && k != 2 && k != 4) ||
+      chunk_bytes <= 0 || chunk_bytes > kMaxChunkBytes || chunk_bytes % 8 || !(threshold > 0.0 && threshold <= 1.0) ||
+      header_bytes < 24 || header_bytes > 24 + 8 * 64 || (header_bytes - 24) % 8 ||
+      (reinterpret_cast<uintptr_t>(x) & 7) || (reinterpret_cast<uintptr_t>(out) & 7))
+    return set_error(ZN_ERR_INVALID, "zn_compress: bad arguments");
+  const int ndim = (header_bytes - 24) / 8;
+  if (out_capacity < zn_compress_bound(n, k, ndim, chunk_bytes))
+    return set_error(ZN_ERR_SPACE, "zn_compress: output buffer too small");
+  const int64_t nch = cdiv(n, chunk_bytes), total = int64_t(k) * nch;
+  if (nch > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_compress: too many chunks");
+  const EncLayout L = enc_layout(total, chunk_bytes, t);
+  if (!temp || temp_bytes < L.total) return set_error(ZN_ERR_SPACE, "zn_compress: temp buffer too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* tb = static_cast<uint8_t*>(temp);
+
+  EncArgs a{};
+  a.x = static_cast<const uint8_t*>(x);
+  a.n = n;
+  a.C = chunk_bytes;
+  a.nch = nch;
+  a.t = t;
+  a.threshold = threshold;
+  a.allow_skip = true;
+  a.meta = tb + L.off_meta;
+  a.meta_slot = L.meta_slot;
+  a.streams = reinterpret_cast<uint16_t*>(tb + L.off_streams);
+  a.unit_words = L.unit_words;
+  a.sub_words = L.sub_words;
+  a.lane_words = L.lane_words;
+  a.comp_bytes = reinterpret_cast<int32_t*>(tb + L.off_comp);
+  a.part_hist = reinterpret_cast<uint32_t*>(tb + L.off_hist);
+  int rc = ZN_OK;
+  if (nch > 0) {
+    switch (k * 2 + (reorder ? 1 : 0)) {
+      case 2: rc = launch_encode<1, false>(a, nch, s); break;
+      case 4: rc = launch_encode<2, false>(a, nch, s); break;
+      case 5: rc = launch_encode<2, true>(a, nch, s); break;
+      case 8: rc = launch_encode<4, false>(a, nch, s); break;
+      case 9: rc = launch_encode<4, true>(a, nch, s); break;
+      default: rc = launch_encode<8, false>(a, nch, s); break;
+    }
+    if (rc) return rc;
+  }
+  ScanArgs sa{};
+  sa.comp_bytes = a.comp_bytes;
+  sa.total = total;
+  sa.nch = nch;
+  sa.C = chunk_bytes;
+  sa.n = n;
+  sa.threshold = threshold;
+  sa.sizes_off = header_bytes;
+  sa.idx_off = header_bytes + 4 * total;
+  sa.out = static_cast<uint8_t*>(out);
+  sa.dst_rel = reinterpret_cast<int64_t*>(tb + L.off_dst);
+  sa.scalars = reinterpret_cast<int64_t*>(tb + L.off_scalars);
+  sa.size_out = size_out;
+  memcpy(sa.header.bytes, header, size_t(header_bytes));
+  sa.header.len = header_bytes;
+  scan_kernel<<<1, kScanThreads, 0, s>>>(sa);
+  count_launch();
+  if ((rc = check_launch("scan_kernel"))) return rc;
+  if (nch == 0) return ZN_OK;
+  PackArgs p{};
+  p.x = a.x;
+  p.n = n;
+  p.C = chunk_bytes;
+  p.nch = nch;
+  p.comp_bytes = a.comp_bytes;
+  p.dst_rel = sa.dst_rel;
+  p.scalars = sa.scalars;
+  p.meta = a.meta;
+  p.meta_slot = a.meta_slot;
+  p.streams = a.streams;
+  p.unit_words = a.unit_words;
+  p.sub_words = a.sub_words;
+  p.lane_words = a.lane_words;
+  p.t = t;
+  p.out = sa.out;
+  switch (k * 2 + (reorder ? 1 : 0)) {
+    case 2: launch_pack<1, false>(p, nch, s); break;
+    case 4: launch_pack<2, false>(p, nch, s); break;
+    case 5: launch_pack<2, true>(p, nch, s); break;
+    case 8: launch_pack<4, false>(p, nch, s); break;
+    case 9: launch_pack<4, true>(p, nch, s); break;
+    default: launch_pack<8, false>(p, nch, s); break;
+  }
+  return check_launch("pack_kernel");
+}
+
+}  // extern "C"

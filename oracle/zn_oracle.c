@@ -122,7 +122,7 @@ int orc_sub_chunks(int64_t chunk_bytes, int64_t sub_chunk_bytes) {
     return (int)count;
 }
 
-/* ---- ZNR1 rANS payload ------------------------------------------------------------------- */
+/* ---- ZNR2 rANS payload ------------------------------------------------------------------- */
 
 void orc_normalize(const uint32_t c[256], int64_t m, uint32_t f[256]) {
     int np = 0, smax = -1;
@@ -157,26 +157,29 @@ void orc_normalize(const uint32_t c[256], int64_t m, uint32_t f[256]) {
 typedef struct {
     int64_t sc;  /* sub-chunk length in symbols (multiple of 128) */
     int nu;      /* non-empty sub-chunks */
-    int lw;      /* bytes per stream-length field */
+    int lw;      /* bytes per stream-length field (one field per state) */
 } ans_geom;
 
 static ans_geom geom(int64_t m, int n_sub) {
     ans_geom g;
     g.sc = cdiv(cdiv(m, n_sub), ROUND) * ROUND;
     g.nu = (int)cdiv(m, g.sc);
-    g.lw = g.sc < 65536 ? 2 : 4;
+    g.lw = g.sc / LANES < 65536 ? 2 : 4; /* a state emits at most one word per symbol */
     return g;
 }
 
 static int64_t table_bytes(int np) { return (2 + 32 + (12 * np + 7) / 8 + 3) & ~(int64_t)3; }
 
+static int64_t lengths_bytes(ans_geom g) { return ((int64_t)g.nu * LANES * g.lw + 3) & ~(int64_t)3; }
+
 static int64_t meta_bytes(int np, ans_geom g) {
-    return table_bytes(np) + ((g.nu * g.lw + 3) & ~3) + (int64_t)g.nu * LANES * 4;
+    return table_bytes(np) + lengths_bytes(g) + (int64_t)g.nu * LANES * 4;
 }
 
 int64_t orc_ans_max_payload(int64_t m, int n_sub) {
-    ans_geom g = geom(m, n_sub);
-    return meta_bytes(256, g) + 2 * m;
+    /* Any unit of at most m symbols: at most n_sub streams with 4-byte lengths, one word per
+     * symbol.  (A shorter unit can have more sub-chunks than a full one.) */
+    return table_bytes(256) + 4 * (int64_t)LANES * n_sub + (int64_t)LANES * 4 * n_sub + 2 * m;
 }
 
 static void put16(uint8_t *p, uint32_t v) { p[0] = (uint8_t)v; p[1] = (uint8_t)(v >> 8); }
@@ -218,47 +221,42 @@ int64_t orc_ans_encode(const uint8_t *sym, int64_t m, int n_sub, uint8_t *out, i
         k++;
     }
     uint8_t *lens = out + tb;
-    uint8_t *states = lens + ((g.nu * g.lw + 3) & ~3);
+    uint8_t *states = lens + lengths_bytes(g);
     int64_t wpos = mb; /* byte offset where the next stream goes */
 
-    uint16_t *tmp = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)(g.sc + 1));
+    /* One word list per state; words are produced last-first and stored first-last. */
+    int64_t per = g.sc / LANES;
+    uint16_t *tmp = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)(LANES * per + 1));
     for (int gi = 0; gi < g.nu; gi++) {
         int64_t base = (int64_t)gi * g.sc;
         int64_t len = m - base < g.sc ? m - base : g.sc;
         int64_t rounds = cdiv(len, ROUND);
         uint32_t x[LANES];
-        for (int l = 0; l < LANES; l++) x[l] = ANS_L;
-        int64_t p_w = g.sc; /* backward write position in tmp */
+        int64_t nw[LANES];
+        for (int l = 0; l < LANES; l++) { x[l] = ANS_L; nw[l] = 0; }
         for (int64_t r = rounds - 1; r >= 0; r--) {
             for (int i = STEPS - 1; i >= 0; i--) {
-                uint16_t w[LANES];
-                int nw = 0;
-                for (int l = 0; l < LANES; l++) {
-                    int64_t p = r * ROUND + l * STEPS + i;
-                    if (p >= len) continue;
-                    uint32_t fs = f[sym[base + p]];
-                    if ((x[l] >> 20) >= fs) { /* x >= fs * 2^20 = ((L >> 12) << 16) * fs */
-                        w[nw++] = (uint16_t)(x[l] & 0xFFFF);
-                        x[l] >>= 16;
-                    }
-                }
-                p_w -= nw;
-                for (int q = 0; q < nw; q++) tmp[p_w + q] = w[q];
                 for (int l = 0; l < LANES; l++) {
                     int64_t p = r * ROUND + l * STEPS + i;
                     if (p >= len) continue;
                     int s = sym[base + p];
+                    if ((x[l] >> 20) >= f[s]) { /* x >= f * 2^20 = ((L >> 12) << 16) * f */
+                        tmp[l * per + nw[l]++] = (uint16_t)(x[l] & 0xFFFF);
+                        x[l] >>= 16;
+                    }
                     x[l] = (x[l] / f[s]) * ANS_M + x[l] % f[s] + cum[s];
                 }
             }
         }
-        int64_t nwords = g.sc - p_w;
-        if (wpos + 2 * nwords > cap) { free(tmp); return -1; }
-        for (int64_t q = 0; q < nwords; q++) put16(out + wpos + 2 * q, tmp[p_w + q]);
-        wpos += 2 * nwords;
-        if (g.lw == 2) put16(lens + 2 * gi, (uint32_t)nwords);
-        else put32(lens + 4 * gi, (uint32_t)nwords);
-        for (int l = 0; l < LANES; l++) put32(states + 4 * ((int64_t)gi * LANES + l), x[l]);
+        for (int l = 0; l < LANES; l++) {
+            if (wpos + 2 * nw[l] > cap) { free(tmp); return -1; }
+            for (int64_t q = 0; q < nw[l]; q++) put16(out + wpos + 2 * q, tmp[l * per + nw[l] - 1 - q]);
+            wpos += 2 * nw[l];
+            int64_t fi = (int64_t)gi * LANES + l;
+            if (g.lw == 2) put16(lens + 2 * fi, (uint32_t)nw[l]);
+            else put32(lens + 4 * fi, (uint32_t)nw[l]);
+            put32(states + 4 * fi, x[l]);
+        }
     }
     free(tmp);
     return wpos;
@@ -296,21 +294,25 @@ int orc_ans_decode(const uint8_t *pl, int64_t size, int64_t m, uint8_t *out) {
     for (int s = 0; s < 256; s++)
         for (uint32_t q = cum[s]; q < cum[s + 1]; q++) slot_sym[q] = (uint8_t)s;
     const uint8_t *lens = pl + tb;
-    const uint8_t *states = lens + ((g.nu * g.lw + 3) & ~3);
+    const uint8_t *states = lens + lengths_bytes(g);
     int64_t spos = mb;
     for (int gi = 0; gi < g.nu; gi++) {
-        int64_t nwords = g.lw == 2 ? get16(lens + 2 * gi) : get32(lens + 4 * gi);
-        if (spos + 2 * nwords > size) return -6;
-        const uint8_t *ws = pl + spos;
-        int64_t ptr = 0;
+        const uint8_t *ws[LANES];
+        int64_t nw[LANES], ptr[LANES];
+        uint32_t x[LANES];
+        for (int l = 0; l < LANES; l++) {
+            int64_t fi = (int64_t)gi * LANES + l;
+            nw[l] = g.lw == 2 ? get16(lens + 2 * fi) : get32(lens + 4 * fi);
+            if (spos + 2 * nw[l] > size) return -6;
+            ws[l] = pl + spos;
+            spos += 2 * nw[l];
+            ptr[l] = 0;
+            x[l] = get32(states + 4 * fi);
+            if (x[l] < ANS_L) return -7;
+        }
         int64_t base = (int64_t)gi * g.sc;
         int64_t len = m - base < g.sc ? m - base : g.sc;
         int64_t rounds = cdiv(len, ROUND);
-        uint32_t x[LANES];
-        for (int l = 0; l < LANES; l++) {
-            x[l] = get32(states + 4 * ((int64_t)gi * LANES + l));
-            if (x[l] < ANS_L) return -7;
-        }
         for (int64_t r = 0; r < rounds; r++) {
             for (int i = 0; i < STEPS; i++) {
                 for (int l = 0; l < LANES; l++) {
@@ -320,22 +322,18 @@ int orc_ans_decode(const uint8_t *pl, int64_t size, int64_t m, uint8_t *out) {
                     int s = slot_sym[slot];
                     out[base + p] = (uint8_t)s;
                     x[l] = f[s] * (x[l] >> ANS_SCALE) + slot - cum[s];
-                }
-                for (int l = 0; l < LANES; l++) {
-                    int64_t p = r * ROUND + l * STEPS + i;
-                    if (p >= len || x[l] >= ANS_L) continue;
-                    if (ptr >= nwords) return -8;
-                    x[l] = (x[l] << 16) | get16(ws + 2 * ptr);
-                    ptr++;
+                    if (x[l] < ANS_L) {
+                        if (ptr[l] >= nw[l]) return -8;
+                        x[l] = (x[l] << 16) | get16(ws[l] + 2 * ptr[l]);
+                        ptr[l]++;
+                    }
                 }
             }
         }
-        if (ptr != nwords) return -9;
         for (int l = 0; l < LANES; l++)
-            if (x[l] != ANS_L) return -10;
-        spos += 2 * nwords;
+            if (ptr[l] != nw[l] || x[l] != ANS_L) return -9;
     }
-    return 0;
+    return spos == size ? 0 : -10;
 }
 
 /* ---- container: src/cuzipnn/_codec.py:1-21, :89-93, :270-306, :361-403, :416-542 ---------- */

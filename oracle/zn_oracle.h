@@ -17,19 +17,19 @@
  *
  * The reference's entropy coder is nvCOMP's batched ANS (nvidia-libnvcomp-cu13 5.3.0.16, a
  * closed binary; call sites src/cuzipnn/_nvcomp.py:179-257).  Its bitstream is not public, so
- * this project defines its own payload format, "ZNR1", built from the published rANS method
+ * this project defines its own payload format, "ZNR2", built from the published rANS method
  * (J. Duda, "Asymmetric numeral systems", 2013; F. Giesen, "Interleaved entropy coders", 2014),
  * and this file is the normative statement of that format:
  *
  *   Scale: 12 bits (M = 4096).  State: u32 in [L, 2^32) with L = 2^16.  I/O: 16-bit words.
  *   A plane chunk of m symbols (1 <= m <= 2^24) is cut into sub-chunks of
  *   sc = roundup(ceil(m / n_sub), 128) symbols; nu = ceil(m / sc) of them are non-empty.
- *   Each sub-chunk is coded by 8 interleaved states ("lanes") that share one word stream.
+ *   Each sub-chunk is coded by 8 interleaved states ("lanes"), each with its own word stream.
  *   Round r, step i (0..15), lane l (0..7) covers symbol r*128 + l*16 + i of the sub-chunk
  *   when that index is below the sub-chunk length.  The decoder runs rounds and steps forward;
- *   at each step every active lane decodes one symbol, then the active lanes whose state fell
- *   below L read one word each, in lane order, from the front of the stream.  The encoder runs
- *   the same schedule backwards (last step first) and writes words from the back.
+ *   a lane decodes its symbol and, if its state fell below L, reads the next word of its own
+ *   stream.  The encoder runs the same schedule backwards (last step first), so each stream is
+ *   stored in the reverse of the order its words were produced.
  *
  *   Frequencies: counts c[s]; np = number of present symbols; smax = most frequent symbol
  *   (lowest index on ties).  np == 1: f[smax] = M.  Otherwise f[s] = max(1, (c*M + m/2) / m)
@@ -42,9 +42,10 @@
  *     [2,34)   presence bitmap, bit (s & 7) of byte (s >> 3)
  *     [34,..)  f[s] - 1 as 12-bit fields for present symbols in ascending order,
  *              field k at bits [12k, 12k+12), zero-padded to a 4-byte boundary
- *     lengths  nu stream lengths in words, u16 if sc < 65536 else u32, padded to 4 bytes
- *     states   nu * 8 u32 final encoder states (the decoder's initial states)
- *     streams  the nu word streams back to back
+ *     lengths  nu * 8 stream lengths in words (sub-chunk-major, then lane), u16 if
+ *              sc / 8 < 65536 else u32, padded to 4 bytes
+ *     states   nu * 8 u32 final encoder states (the decoder's initial states), same order
+ *     streams  the nu * 8 word streams back to back, same order
  */
 #ifndef ZN_ORACLE_H
 #define ZN_ORACLE_H
@@ -80,7 +81,7 @@ void orc_crc32_segments(const uint8_t *p, int64_t n, int64_t seg, uint32_t *out)
 
 int orc_sub_chunks(int64_t chunk_bytes, int64_t sub_chunk_bytes);
 
-/* Frequency normalisation of the ZNR1 format (exposed for tests). */
+/* Frequency normalisation of the ZNR2 format (exposed for tests). */
 void orc_normalize(const uint32_t counts[256], int64_t m, uint32_t freqs[256]);
 
 int64_t orc_ans_max_payload(int64_t m, int n_sub);

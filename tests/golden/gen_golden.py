@@ -8,7 +8,7 @@ It imports, from the reference checkout (ruihe774/cuZipNN):
   - src/cuzipnn/_kernels.py, run by Triton's CPU interpreter (TRITON_INTERPRET=1), for the
     byte-plane split / merge / chunk-copy vectors;
   - src/cuzipnn/_codec.py, run on the CPU, for whole blobs.  Its entropy coder (nvCOMP, absent)
-    is replaced by a stand-in module that calls the oracle's ZNR1 rANS coder, so each blob is
+    is replaced by a stand-in module that calls the oracle's ZNR2 rANS coder, so each blob is
     the reference's container, passthrough rule, tables, padding and CRC logic wrapped around
     the oracle's payloads.  The oracle's own compressor must reproduce these blobs byte for
     byte (with the version byte set to the reference's 2).

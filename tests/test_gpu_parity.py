@@ -1,0 +1,222 @@
+"""CUDA path against the oracle and the reference-generated golden vectors (bit-exact).
+
+Every test here runs the library through its C ABI (via the package's ctypes binding) on a GPU
+and compares bytes: blobs against the reference container produced by the reference's own
+_codec.py (tests/golden), ZNR2 payloads against the oracle's encoder, planes against the
+reference's Triton split, CRCs against zlib.
+"""
+
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+_TORCH = {
+    "bool": torch.bool, "uint8": torch.uint8, "int8": torch.int8, "int16": torch.int16,
+    "int32": torch.int32, "int64": torch.int64, "float16": torch.float16,
+    "bfloat16": torch.bfloat16, "float32": torch.float32, "float64": torch.float64,
+    "float8_e4m3fn": torch.float8_e4m3fn, "float8_e5m2": torch.float8_e5m2,
+    "uint16": torch.uint16, "uint32": torch.uint32, "uint64": torch.uint64,
+    "complex64": torch.complex64,
+}
+
+
+def _tensor(raw: np.ndarray, dtype: str, shape) -> torch.Tensor:
+    if raw.size == 0:
+        return torch.empty(tuple(shape), dtype=_TORCH[dtype])
+    t = torch.from_numpy(raw.copy()).view(_TORCH[dtype])
+    return t.reshape(tuple(shape))
+
+
+def _u8(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu().contiguous().reshape(-1)
+    return t.view(torch.uint8).numpy() if t.numel() else np.zeros(0, np.uint8)
+
+
+def _blob_names(golden):
+    return sorted({k.split("/")[1] for k in golden if k.startswith("blob/")})
+
+
+@pytest.fixture(scope="module")
+def z():
+    import cuzipnn_b200
+
+    return cuzipnn_b200
+
+
+def test_blobs_equal_reference_container(golden, z):
+    """compress_tensor on the GPU == the reference's _codec.py blob (version byte 3)."""
+    for name in _blob_names(golden):
+        raw = golden[f"blob/{name}/x"]
+        dtype = golden[f"blob/{name}/dtype"].tobytes().decode()
+        shape = golden[f"blob/{name}/shape"].tolist()
+        chunk, sub, minc = golden[f"blob/{name}/kw"].tolist()
+        thr = float(golden[f"blob/{name}/thr"][0])
+        ref = golden[f"blob/{name}/blob"].copy()
+        ref[4] = 3
+        x = _tensor(raw, dtype, shape).cuda()
+        blob = z.compress_tensor(x, chunk_bytes=chunk, sub_chunk_bytes=sub, passthrough_threshold=thr,
+                                 min_compress_bytes=minc)
+        assert np.array_equal(_u8(blob), ref), name
+        y = z.decompress_tensor(blob)
+        assert y.dtype == x.dtype and tuple(y.shape) == tuple(x.shape)
+        assert np.array_equal(_u8(y), raw), name
+        assert z.last_decode_status() == 0, name
+
+
+@pytest.mark.parametrize(
+    "dtype,n,chunk,sub",
+    [
+        ("bfloat16", 1_000_003, 131072, 8192),
+        ("float32", 300_001, 131072, 8192),
+        ("float16", 500_000, 4096, 1000),
+        ("float8_e4m3fn", 700_001, 131072, 2048),
+        ("bfloat16", 262144, 131072, 1 << 30),
+        ("bfloat16", 200_000, 640, 8192),
+        ("int32", 100_000, 4096, 8192),
+        ("float64", 50_000, 4096, 8192),
+    ],
+)
+def test_gpu_blob_equals_oracle(z, dtype, n, chunk, sub):
+    g = torch.Generator().manual_seed(n)
+    if dtype.startswith("float8"):
+        x = (torch.randn(n, generator=g) * 16).clamp(-448, 448).to(_TORCH[dtype])
+    elif dtype == "int32":
+        x = torch.randint(-1000, 1000, (n,), generator=g, dtype=torch.int32)
+    else:
+        x = (torch.randn(n, generator=g) * 0.02).to(_TORCH[dtype])
+    ref = O.compress(_u8(x), x.shape, dtype, chunk_bytes=chunk, sub_chunk_bytes=sub, min_compress_bytes=0,
+                     threads=8)
+    blob = z.compress_tensor(x.cuda(), chunk_bytes=chunk, sub_chunk_bytes=sub, min_compress_bytes=0)
+    assert np.array_equal(_u8(blob), np.frombuffer(ref, dtype=np.uint8))
+    assert np.array_equal(_u8(z.decompress_tensor(blob)), _u8(x))
+    # And the GPU decodes the oracle's blob.
+    y = z.decompress_tensor(torch.frombuffer(bytearray(ref), dtype=torch.uint8).cuda())
+    assert np.array_equal(_u8(y), _u8(x))
+
+
+def test_split_matches_reference(golden):
+    from cuzipnn_b200 import _kernels
+
+    for kind in sorted({k.split("/")[1] for k in golden if k.startswith("split/")}):
+        n, k, reorder, stride = golden[f"split/{kind}/meta"].tolist()
+        x = torch.from_numpy(golden[f"split/{kind}/x"].copy()).cuda()
+        x = x.view({1: torch.uint8, 2: torch.int16, 4: torch.int32, 8: torch.int64}[k])
+        planar = torch.zeros(k * stride, dtype=torch.uint8, device="cuda")
+        _kernels.split(x, planar, stride, bool(reorder))
+        assert np.array_equal(planar.cpu().numpy(), golden[f"split/{kind}/planar"]), kind
+
+
+def test_merge_matches_reference(golden):
+    from cuzipnn_b200 import _kernels
+
+    for kind in sorted({k.split("/")[1] for k in golden if k.startswith("merge/")}):
+        n, k, reorder, chunk = golden[f"merge/{kind}/meta"].tolist()
+        base = torch.from_numpy(golden[f"merge/{kind}/base"].copy()).cuda()
+        tbl = torch.from_numpy(golden[f"merge/{kind}/tbl"].copy()).cuda()
+        out = torch.empty(n * k, dtype=torch.uint8, device="cuda")
+        out = out.view({1: torch.uint8, 2: torch.int16, 4: torch.int32, 8: torch.int64}[k])
+        _kernels.merge(tbl, base, out, chunk, bool(reorder))
+        assert np.array_equal(_u8(out), golden[f"merge/{kind}/out"]), kind
+
+
+@pytest.mark.parametrize("pad", [False, True])
+def test_copy_chunks_matches_reference(golden, pad):
+    from cuzipnn_b200 import _kernels
+
+    key = "copy/pad" if pad else "copy/nopad"
+    src = torch.from_numpy(golden[key + "/src"].copy()).cuda()
+    dst = torch.full((80 * 1024,), 0xA5, dtype=torch.uint8, device="cuda")
+    soff = torch.from_numpy(golden[key + "/soff"].copy()).cuda()
+    doff = torch.from_numpy(golden[key + "/doff"].copy()).cuda()
+    sizes = torch.from_numpy(golden[key + "/sizes"].copy()).cuda()
+    _kernels.copy_chunks(src.data_ptr() + soff, dst.data_ptr() + doff, sizes, 12345, pad)
+    assert np.array_equal(dst.cpu().numpy(), golden[key + "/dst"])
+
+
+def test_crc_matches_reference_and_zlib(golden, z):
+    from cuzipnn_b200 import _codec
+
+    for key in [k for k in golden if k.startswith("crc/")]:
+        _, name, seg = key.split("/")
+        blob = golden[f"blob/{name}/blob"].copy()
+        blob[4] = 3
+        d = torch.from_numpy(blob).cuda()
+        crc = _codec._crc32(d, int(seg)).cpu().numpy()
+        # The golden CRCs are of the version-2 blob; the version byte sits in the first segment.
+        ref = golden[key].copy()
+        ref[0] = zlib.crc32(blob[: int(seg)].tobytes())
+        assert np.array_equal(crc, ref), key
+
+
+@pytest.mark.parametrize("nbytes", [0, 1, 7, 8, 127, 128, 129, 4096, 100_003, 1 << 20, (1 << 20) + 13])
+@pytest.mark.parametrize("seg", [1, 8, 100, 1000, 16384, 32768, 32769, 100_000, 1 << 30])
+def test_crc_sizes(nbytes, seg):
+    from cuzipnn_b200 import _codec
+
+    data = np.random.default_rng(nbytes + seg).integers(0, 256, nbytes + 5, dtype=np.uint8)
+    for off in (0, 3):
+        d = torch.from_numpy(data[off : off + nbytes].copy())
+        buf = torch.empty(nbytes + 16, dtype=torch.uint8, device="cuda")
+        view = buf[off : off + nbytes]
+        view.copy_(d)
+        crc = _codec._crc32(view, seg).cpu().numpy()
+        ref = [zlib.crc32(data[off + i : off + min(i + seg, nbytes)].tobytes()) for i in range(0, nbytes, seg)]
+        assert crc.tolist() == ref, (nbytes, seg, off)
+
+
+@pytest.mark.parametrize("sub_chunks", [4, 16, 64])
+def test_ans_seam_matches_oracle(sub_chunks):
+    from cuzipnn_b200 import _ans
+
+    rng = np.random.default_rng(sub_chunks)
+    chunk = 131072
+    sizes = [chunk, 1, 8, 4099, 100_000, chunk]
+    bufs = [np.clip(rng.normal(0, 6, s) + 120, 0, 255).astype(np.uint8) for s in sizes]
+    bufs[-1] = rng.integers(0, 256, chunk, dtype=np.uint8)
+    inp = [torch.from_numpy(b).cuda() for b in bufs]
+    slot = _ans.max_compressed_chunk_bytes(chunk, sub_chunks)
+    outs = [torch.zeros(slot, dtype=torch.uint8, device="cuda") for _ in inp]
+    in_ptrs = torch.tensor([t.data_ptr() for t in inp], dtype=torch.int64, device="cuda")
+    in_bytes = torch.tensor(sizes, dtype=torch.int64, device="cuda")
+    out_ptrs = torch.tensor([t.data_ptr() for t in outs], dtype=torch.int64, device="cuda")
+    out_bytes = torch.empty(len(inp), dtype=torch.int64, device="cuda")
+    statuses = torch.empty(len(inp), dtype=torch.int32, device="cuda")
+    _ans.compress(in_ptrs, in_bytes, chunk, sum(sizes), out_ptrs, out_bytes, statuses, sub_chunks)
+    assert statuses.cpu().tolist() == [0] * len(inp)
+    for b, o, nb in zip(bufs, outs, out_bytes.cpu().tolist()):
+        assert o[:nb].cpu().numpy().tobytes() == O.ans_encode(b, sub_chunks)
+    dec = [torch.zeros(s, dtype=torch.uint8, device="cuda") for s in sizes]
+    st = _ans.decompress(out_ptrs, out_bytes, in_bytes, chunk, sum(sizes),
+                         torch.tensor([t.data_ptr() for t in dec], dtype=torch.int64, device="cuda"))
+    assert st.cpu().tolist() == [0] * len(inp)
+    for b, d in zip(bufs, dec):
+        assert np.array_equal(d.cpu().numpy(), b)
+
+
+def test_corrupt_blob_sets_status_without_fault(z):
+    """A damaged payload is reported through the status word; the GPU keeps working."""
+    x = (torch.randn(300_000, device="cuda") * 0.02).to(torch.bfloat16)
+    blob = z.compress_tensor(x, chunk_bytes=4096, min_compress_bytes=0)
+    bad = blob.clone()
+    n = bad.numel()
+    bad[n // 2 : n // 2 + 64] ^= 0x5A  # inside some payload or raw unit
+    y = z.decompress_tensor(bad)
+    torch.cuda.synchronize()
+    status = z.last_decode_status()
+    # Either the damage hit raw bytes (decodes, differs) or a payload (status set).
+    assert status != 0 or not torch.equal(y.view(torch.int16), x.view(torch.int16))
+    # Truncated tables: stored sizes pointing past the end of the blob.
+    bad2 = blob.clone()
+    bad2[40:44] = torch.tensor([0xFF, 0xFF, 0xFF, 0x7F], dtype=torch.uint8)
+    z.decompress_tensor(bad2)
+    assert z.last_decode_status() != 0
+    with pytest.raises(ValueError, match="corrupt"):
+        z.decompress_tensor(bad2, readback_to_cpu=True)
+    # The context is still usable.
+    assert torch.equal(z.decompress_tensor(blob).view(torch.int16), x.view(torch.int16))

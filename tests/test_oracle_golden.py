@@ -3,7 +3,7 @@
 Pins every oracle piece that has a reference counterpart: the byte planes of the Triton split
 (src/cuzipnn/_kernels.py:34-54), the merge (:57-105), the chunk copy (:108-131), the sub-chunk
 count (src/cuzipnn/_codec.py:83-86), the passthrough budgets (:74-80), whole blobs of the
-reference container around ZNR1 payloads (:231-413) and their CRC-32s (:116-147).
+reference container around ZNR2 payloads (:231-413) and their CRC-32s (:116-147).
 """
 
 import zlib
