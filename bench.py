@@ -1,0 +1,417 @@
+#!/usr/bin/env python
+"""Benchmark of the codec path on the 7B bf16 GQA decoder configuration.
+
+Workload (per GPU): the weights of a 7B GQA decoder in bfloat16 -- 28 layers, hidden 3584, SwiGLU
+MLP 18944, 28 query / 4 KV heads of dim 128 with q/k/v biases, RMSNorm vectors of ones, untied
+embedding and LM head over a 152064 vocabulary: 339 tensors, 15.23 GB.  Matrices and biases are
+N(0, 0.02) seeded per tensor (seed = tensor index), generated on the GPU; there is no checkpoint.
+
+A step compresses every tensor (compress_tensors, blobs kept on the GPU) and decompresses every
+blob (decompress_tensors): value = original bytes of all GPUs / step time, in GB/s (1e9).  The
+inputs (15 GB) are far larger than the 126 MB L2, so no flush is needed between steps.  With
+torchrun each rank processes its own copy of the model (weak scaling); times are the max over
+ranks.
+
+--impl reference times the reference's CPU arm: the repository's C restatement of the codec path
+(oracle/, the checker), on all host cores, on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+GB = 1e9
+HIDDEN, INTER, LAYERS, VOCAB, HEADS, KV_HEADS, HEAD_DIM = 3584, 18944, 28, 152064, 28, 4, 128
+WORKLOAD = (
+    "7B GQA decoder bf16 weights: 28 layers, hidden 3584, SwiGLU 18944, 28 q / 4 kv heads x 128 with "
+    "q/k/v biases, RMSNorm ones, untied embedding + LM head, vocab 152064; 339 tensors, 15.23 GB; "
+    "compress_tensors + decompress_tensors (defaults: chunk_bytes 131072, sub_chunk_bytes 8192, "
+    "passthrough 0.95, min_compress_bytes 65536)"
+)
+
+
+def model_shapes() -> list[tuple[str, tuple[int, ...], str]]:
+    """(name, shape, init) of the 7B bf16 decoder, in checkpoint order."""
+    kv = KV_HEADS * HEAD_DIM
+    out = [("model.embed_tokens.weight", (VOCAB, HIDDEN), "normal")]
+    for i in range(LAYERS):
+        p = f"model.layers.{i}."
+        out += [
+            (p + "self_attn.q_proj.weight", (HIDDEN, HIDDEN), "normal"),
+            (p + "self_attn.q_proj.bias", (HIDDEN,), "normal"),
+            (p + "self_attn.k_proj.weight", (kv, HIDDEN), "normal"),
+            (p + "self_attn.k_proj.bias", (kv,), "normal"),
+            (p + "self_attn.v_proj.weight", (kv, HIDDEN), "normal"),
+            (p + "self_attn.v_proj.bias", (kv,), "normal"),
+            (p + "self_attn.o_proj.weight", (HIDDEN, HIDDEN), "normal"),
+            (p + "mlp.gate_proj.weight", (INTER, HIDDEN), "normal"),
+            (p + "mlp.up_proj.weight", (INTER, HIDDEN), "normal"),
+            (p + "mlp.down_proj.weight", (HIDDEN, INTER), "normal"),
+            (p + "input_layernorm.weight", (HIDDEN,), "ones"),
+            (p + "post_attention_layernorm.weight", (HIDDEN,), "ones"),
+        ]
+    out += [("model.norm.weight", (HIDDEN,), "ones"), ("lm_head.weight", (VOCAB, HIDDEN), "normal")]
+    return out
+
+
+def make_tensor(idx: int, shape, init: str, device) -> torch.Tensor:
+    if init == "ones":
+        return torch.ones(shape, dtype=torch.bfloat16, device=device)
+    g = torch.Generator(device=device).manual_seed(idx)
+    return (torch.randn(shape, generator=g, device=device) * 0.02).to(torch.bfloat16)
+
+
+def build_model(device) -> list[torch.Tensor]:
+    return [make_tensor(i, s, init, device) for i, (_, s, init) in enumerate(model_shapes())]
+
+
+def nbytes(ts) -> int:
+    return sum(t.numel() * t.element_size() for t in ts)
+
+
+# ---- measurement helpers ----------------------------------------------------------------------
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock, power and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in open(self.path):
+                f = [v.strip() for v in line.split(",")]
+                if len(f) >= 9 and f[1].replace(".", "").isdigit():
+                    rows.append(f)
+            os.unlink(self.path)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = sorted(float(r[1]) for r in rows)
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][2]), "reasons": sorted(reasons),
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+def measured_hbm_peak() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(path))["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s"
+
+
+def profile_traffic(kernel: str) -> dict | None:
+    """DRAM traffic per algorithmic byte of a kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_traffic.json")
+    try:
+        return json.load(open(path))
+    except (OSError, ValueError):
+        return None
+
+
+def cpu_round_trip(tensors, threads: int) -> tuple[float, float, int, int]:
+    """The oracle's compress + decompress of host tensors: (compress s, decompress s, in, out bytes)."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    raws = [t.cpu().contiguous().view(torch.int16).numpy().view(np.uint8) for t in tensors]
+    t0 = time.perf_counter()
+    blobs = [O.compress(r, t.shape, "bfloat16", threads=threads) for r, t in zip(raws, tensors)]
+    t1 = time.perf_counter()
+    for b, r in zip(blobs, raws):
+        y = O.decompress(b, threads=threads)
+        assert y.size == r.size
+    t2 = time.perf_counter()
+    return t1 - t0, t2 - t1, sum(r.size for r in raws), sum(len(b) for b in blobs)
+
+
+def cpu_sample(device="cpu") -> list[torch.Tensor]:
+    """Layer 0 of the model (q/k/v/o, gate/up/down, biases, norms): 466 MB, every tensor kind."""
+    shapes = model_shapes()
+    return [make_tensor(i, s, init, device) for i, (n, s, init) in enumerate(shapes) if ".layers.0." in n]
+
+
+# ---- the reference arm --------------------------------------------------------------------------
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    sample = cpu_sample()
+    times = []
+    for step in range(args.warmup + args.steps):
+        tc, td, nin, nout = cpu_round_trip(sample, threads)
+        if step >= args.warmup:
+            times.append(tc + td)
+    t = sum(times) / len(times)
+    value = nin / t / GB
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u8",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": "layer 0 (466 MB) per step", "ratio": round(nout / nin, 5)},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "compress + decompress of layer 0 (466 MB) with the C oracle (OpenMP)"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "compress / decompress GB/s (original bytes) per B200 and 8-GPU box; ratio"
+
+
+# ---- our arm ----------------------------------------------------------------------------------
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import cuzipnn_b200 as z
+    from cuzipnn_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    model = build_model(device)
+    model_bytes = nbytes(model)
+    torch.cuda.synchronize()
+
+    def step():
+        blobs = z.compress_tensors(model, readback_to_cpu=False)
+        mid = torch.cuda.Event(enable_timing=True)
+        mid.record()
+        outs = z.decompress_tensors(blobs)
+        return blobs, outs, mid
+
+    # Correctness once, outside the timed region.
+    blobs, outs, _ = step()
+    for i in (0, 1, 8, 338):
+        assert torch.equal(outs[i].view(torch.int16), model[i].view(torch.int16)), i
+    assert z.last_decode_status(device) == 0
+    blob_bytes = sum(b.numel() for b in blobs)
+    ratio = blob_bytes / model_bytes
+    del blobs, outs
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    launches0 = _lib.launch_count()
+    ev = []
+    with ClockSampler(local) as clocks, _lib.KernelTimer() as kt:
+        barrier()
+        for _ in range(args.steps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            blobs, outs, mid = step()
+            b.record()
+            ev.append((a, mid, b))
+            del blobs, outs
+        barrier()
+    gpu_launches = _lib.launch_count() - launches0
+    t_step = sum(a.elapsed_time(b) for a, _, b in ev) / len(ev) / 1e3
+    t_comp = sum(a.elapsed_time(m) for a, m, _ in ev) / len(ev) / 1e3
+    t_dec = sum(m.elapsed_time(b) for _, m, b in ev) / len(ev) / 1e3
+    t_step, t_comp, t_dec = (max_over_ranks(v) for v in (t_step, t_comp, t_dec))
+    value = world * model_bytes / t_step / GB
+
+    # Roofline of the dominant kernel (largest summed device time in the timed region).
+    times = kt.times
+    dominant = max(times, key=lambda k: times[k][0])
+    dom_ms, dom_n = times[dominant]
+    per_launch_s = dom_ms / dom_n / 1e3
+    coded = [t for t in model if t.numel() * t.element_size() >= 65536]
+    coded_bytes = nbytes(coded)
+    coded_blob = blob_bytes - (model_bytes - coded_bytes)  # stored blobs add header bytes only
+    # Algorithmic bytes per launch: every launch of this kernel covers all non-stored tensors.
+    algo = {"decode": coded_blob + coded_bytes, "encode": coded_bytes + coded_blob,
+            "hist": coded_bytes, "pack": coded_bytes + coded_blob}.get(dominant, coded_bytes)
+    peak, peak_src = measured_hbm_peak()
+    achieved = algo / per_launch_s / GB
+    tr = profile_traffic(dominant + "_kernel")
+    traffic = round(tr["traffic_per_algo_byte"] * algo) if tr else None
+    roofline = {"bound": "hbm", "kernel": dominant + "_kernel", "achieved": round(achieved, 1),
+                "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "traffic": traffic, "algo_bytes_per_launch": algo,
+                "launch_ms": round(per_launch_s * 1e3, 4),
+                "kernel_share": {k: round(v[0] / sum(x[0] for x in times.values()), 4) for k, v in times.items()}}
+
+    # One tensor at a time (the reference's own methodology), device time.
+    ev1 = []
+    for _ in range(1):
+        a = torch.cuda.Event(enable_timing=True)
+        m = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        bl = [z.compress_tensor(t, readback_to_cpu=False) for t in model]
+        m.record()
+        for x in bl:
+            z.decompress_tensor(x)
+        b.record()
+        torch.cuda.synchronize()
+        ev1.append((a.elapsed_time(m) / 1e3, m.elapsed_time(b) / 1e3))
+        del bl
+    one_c = max_over_ranks(min(v[0] for v in ev1))
+    one_d = max_over_ranks(min(v[1] for v in ev1))
+
+    # End to end through the public API from pinned host memory: H2D of the inputs, CPU blobs,
+    # H2D of the blobs, and a D2H read of a result word each step.
+    host = [t.cpu().pin_memory() for t in model]
+    torch.cuda.synchronize()
+    barrier()
+    e2e_times = []
+    h2d = d2h = 0
+    for s_i in range(args.e2e_steps + 1):
+        t0 = time.perf_counter()
+        cblobs = z.compress_tensors(host, readback_to_cpu=True, pin_memory=True)
+        outs = z.decompress_tensors(cblobs)
+        check = outs[-1].view(-1)[:4].view(torch.uint8).cpu()
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        if s_i:  # the first pass warms the pinned-memory pools
+            e2e_times.append(t1 - t0)
+        sz = sum(b.numel() for b in cblobs)
+        h2d, d2h = model_bytes + sz, sz + check.numel()
+        del cblobs, outs
+    del host
+    t_e2e = max_over_ranks(sum(e2e_times) / len(e2e_times))
+    e2e = {"value": round(world * model_bytes / t_e2e / GB, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e * 1e3, 1),
+           "path": "pinned host tensors -> compress_tensors(readback_to_cpu, pin_memory) -> decompress_tensors"}
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        tc, td, nin, _ = cpu_round_trip(cpu_sample(), threads)
+        cpu_baseline = {"value": round(nin / (tc + td) / GB, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                        "sample": "compress + decompress of layer 0 (466 MB) with the C oracle (OpenMP)"}
+
+    barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(t_step * 1e3, 3),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "u8",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "value": "original bytes / (compress + decompress time)",
+                       "l2": "inputs 15.2 GB per GPU >> 126 MB L2 (no flush)", "parallelism": f"{world} x replica"},
+            "compress_gbs": round(world * model_bytes / t_comp / GB, 3),
+            "decompress_gbs": round(world * model_bytes / t_dec / GB, 3),
+            "ratio": round(ratio, 5),
+            "one_tensor_at_a_time": {"compress_gbs": round(world * model_bytes / one_c / GB, 3),
+                                     "decompress_gbs": round(world * model_bytes / one_d / GB, 3)},
+            "roofline": roofline,
+            "cpu_baseline": cpu_baseline,
+            "clocks": clocks.summary(),
+            "e2e": e2e,
+            "gpu_launches": gpu_launches,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

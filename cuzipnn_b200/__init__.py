@@ -4,7 +4,9 @@ src/cuzipnn/__init__.py) on hand-written sm_100a kernels, with rANS as the entro
 from ._codec import (
     compress_tensor,
     compress_tensor_with_crc32,
+    compress_tensors,
     decompress_tensor,
+    decompress_tensors,
     hash_tensor_with_crc32,
     last_decode_status,
 )
@@ -12,7 +14,9 @@ from ._codec import (
 __all__ = [
     "compress_tensor",
     "compress_tensor_with_crc32",
+    "compress_tensors",
     "decompress_tensor",
+    "decompress_tensors",
     "hash_tensor_with_crc32",
     "last_decode_status",
 ]

@@ -46,9 +46,12 @@ def decompress(in_ptrs, in_bytes, out_capacity, chunk_bytes, total_bytes, out_pt
     Returns the int32 per-chunk statuses (the reference allocates them but never reads them)."""
     n = in_ptrs.numel()
     statuses = torch.empty(n, dtype=torch.int32, device=in_ptrs.device)
+    tb = int(_lib.lib.zn_ans_decompress_temp_bytes(n))
+    temp = torch.empty(max(tb, 1), dtype=torch.uint8, device=in_ptrs.device)
     _lib.check(
         _lib.lib.zn_ans_decompress(in_ptrs.data_ptr(), in_bytes.data_ptr(), out_capacity.data_ptr(), n,
-                                   out_ptrs.data_ptr(), statuses.data_ptr(), None, 0, _stream(in_ptrs)),
+                                   out_ptrs.data_ptr(), statuses.data_ptr(), temp.data_ptr(), tb,
+                                   _stream(in_ptrs)),
         "zn_ans_decompress",
     )
     return statuses

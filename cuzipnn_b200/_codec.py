@@ -237,6 +237,39 @@ def hash_tensor_with_crc32(
         return crc.cpu() if readback_to_cpu else crc
 
 
+def _check_args(
+    tensor: torch.Tensor,
+    chunk_bytes: int,
+    sub_chunk_bytes: int,
+    passthrough_threshold: float,
+    min_compress_bytes: int,
+    checksum_chunk_bytes: int | None,
+    pin_memory: bool,
+    compute_device: torch.device | str | None,
+    readback_to_cpu: bool,
+) -> tuple[torch.device | None, int]:
+    """Argument checks in the reference's order and wording (_codec.py:243-262)."""
+    compute_device = _check_device(compute_device)
+    if pin_memory and not readback_to_cpu:
+        raise ValueError("pin_memory requires readback_to_cpu")
+    if tensor.dtype not in _CODES:
+        raise TypeError(f"unsupported dtype {tensor.dtype}")
+    if chunk_bytes % 8 or not 0 < chunk_bytes <= MAX_CHUNK_BYTES:
+        raise ValueError(f"chunk_bytes must be a multiple of 8 in (0, {MAX_CHUNK_BYTES}]")
+    if passthrough_threshold <= 0 or passthrough_threshold > 1:
+        raise ValueError("passthrough_threshold must be in (0, 1]")
+    if sub_chunk_bytes <= 0:
+        raise ValueError("sub_chunk_bytes must be positive")
+    if min_compress_bytes < 0:
+        raise ValueError("min_compress_bytes must be non-negative")
+    if checksum_chunk_bytes is not None and checksum_chunk_bytes <= 0:
+        raise ValueError("checksum_chunk_bytes must be positive")
+    sub_chunks = _sub_chunks(chunk_bytes, sub_chunk_bytes)
+    if tensor.dim() > _MAX_NDIM:
+        raise ValueError(f"at most {_MAX_NDIM} dimensions are supported")
+    return compute_device, sub_chunks
+
+
 def _header(tensor: torch.Tensor, flags: int, chunk_bytes: int, n_comp: int) -> bytes:
     """The fixed header and shape (_codec.py:270-292)."""
     fixed = _FIXED.pack(
@@ -257,25 +290,10 @@ def _compress(
     compute_device: torch.device | str | None,
     readback_to_cpu: bool,
 ) -> tuple[torch.Tensor, torch.Tensor | None]:
-    # Argument checks in the reference's order and wording (_codec.py:243-262).
-    compute_device = _check_device(compute_device)
-    if pin_memory and not readback_to_cpu:
-        raise ValueError("pin_memory requires readback_to_cpu")
-    if tensor.dtype not in _CODES:
-        raise TypeError(f"unsupported dtype {tensor.dtype}")
-    if chunk_bytes % 8 or not 0 < chunk_bytes <= MAX_CHUNK_BYTES:
-        raise ValueError(f"chunk_bytes must be a multiple of 8 in (0, {MAX_CHUNK_BYTES}]")
-    if passthrough_threshold <= 0 or passthrough_threshold > 1:
-        raise ValueError("passthrough_threshold must be in (0, 1]")
-    if sub_chunk_bytes <= 0:
-        raise ValueError("sub_chunk_bytes must be positive")
-    if min_compress_bytes < 0:
-        raise ValueError("min_compress_bytes must be non-negative")
-    if checksum_chunk_bytes is not None and checksum_chunk_bytes <= 0:
-        raise ValueError("checksum_chunk_bytes must be positive")
-    sub_chunks = _sub_chunks(chunk_bytes, sub_chunk_bytes)
-    if tensor.dim() > _MAX_NDIM:
-        raise ValueError(f"at most {_MAX_NDIM} dimensions are supported")
+    compute_device, sub_chunks = _check_args(
+        tensor, chunk_bytes, sub_chunk_bytes, passthrough_threshold, min_compress_bytes,
+        checksum_chunk_bytes, pin_memory, compute_device, readback_to_cpu,
+    )
 
     x = tensor.detach()
     k, n, reorder = x.element_size(), x.numel(), x.dtype in _REORDER
@@ -358,7 +376,12 @@ def last_decode_status(device: torch.device | str | int | None = None) -> int:
     if dev.type == "cuda" and dev.index is None:
         dev = torch.device("cuda", torch.cuda.current_device())
     st = _LAST_STATUS.get(dev.index if dev.type == "cuda" else int(dev))
-    return 0 if st is None else int(st.item())
+    if st is None:
+        return 0
+    bits = 0
+    for v in st.cpu().tolist():  # one word per blob of the latest call: OR them
+        bits |= int(v)
+    return bits
 
 
 def decompress_tensor(
@@ -443,6 +466,196 @@ def decompress_tensor(
                 raise ValueError(f"blob is corrupt (decoder status {int(status.item())})")
 
         return out
+
+
+def _ptr_array(ctype, values):
+    return (ctype * len(values))(*values)
+
+
+def compress_tensors(
+    tensors: list[torch.Tensor],
+    *,
+    chunk_bytes: int = DEFAULT_CHUNK_BYTES,
+    sub_chunk_bytes: int = DEFAULT_SUB_CHUNK_BYTES,
+    passthrough_threshold: float = DEFAULT_PASSTHROUGH_THRESHOLD,
+    min_compress_bytes: int = DEFAULT_MIN_COMPRESS_BYTES,
+    pin_memory: bool = False,
+    compute_device: torch.device | str | None = None,
+    readback_to_cpu: bool = True,
+) -> list[torch.Tensor]:
+    """compress_tensor over a list of tensors, with one kernel launch per stage for all tensors of
+    an element size (and one host synchronization in all).  Each blob equals compress_tensor's.
+
+    With readback_to_cpu=False the blobs are views into one shared GPU buffer."""
+    blobs: list[torch.Tensor | None] = [None] * len(tensors)
+    groups: dict[tuple[int, bool], list[int]] = {}
+    sub_chunks = _sub_chunks(chunk_bytes, sub_chunk_bytes) if sub_chunk_bytes > 0 else 0
+    for i, t in enumerate(tensors):
+        dev, sub_chunks = _check_args(t, chunk_bytes, sub_chunk_bytes, passthrough_threshold, min_compress_bytes,
+                                      None, pin_memory, compute_device, readback_to_cpu)
+        k, n = t.element_size(), t.numel()
+        if n * k < min_compress_bytes or n == 0:
+            blobs[i] = compress_tensor(t, chunk_bytes=chunk_bytes, sub_chunk_bytes=sub_chunk_bytes,
+                                       passthrough_threshold=passthrough_threshold,
+                                       min_compress_bytes=min_compress_bytes, pin_memory=pin_memory,
+                                       compute_device=compute_device, readback_to_cpu=readback_to_cpu)
+        else:
+            groups.setdefault((k, t.dtype in _REORDER), []).append(i)
+    if not groups:
+        return blobs  # type: ignore[return-value]
+    first = tensors[next(iter(groups.values()))[0]]
+    device = _gpu(first.detach(), _check_device(compute_device))
+    pending = []
+    with torch.cuda.device(device):
+        stream = _stream(device)
+        for (k, reorder), idx in groups.items():
+            xs, heads, caps, offs = [], [], [], []
+            total_cap = 0
+            for i in idx:
+                x = tensors[i].detach()
+                x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous().view(-1)
+                if x.data_ptr() % 16:
+                    x = x.clone()
+                xs.append(x)
+                heads.append(_header(tensors[i], _FLAG_REORDER if reorder else 0, chunk_bytes, 0))
+                cap = int(_lib.lib.zn_compress_bound(x.numel(), k, tensors[i].dim(), chunk_bytes))
+                caps.append(cap)
+                offs.append(total_cap)
+                total_cap += (cap + 255) & ~255
+            out = torch.empty(total_cap, dtype=torch.uint8, device=device)
+            sizes = torch.empty(len(idx), dtype=torch.int64, device=device)
+            nj = len(idx)
+            n_arr = _ptr_array(ctypes.c_int64, [x.numel() for x in xs])
+            tb = int(_lib.lib.zn_compress_batch_temp_bytes(nj, n_arr, k, chunk_bytes, sub_chunks))
+            temp = torch.empty(max(tb, 1), dtype=torch.uint8, device=device)
+            hbufs = [ctypes.create_string_buffer(h, len(h)) for h in heads]
+            _lib.check(
+                _lib.lib.zn_compress_batch(
+                    nj, _ptr_array(ctypes.c_void_p, [x.data_ptr() for x in xs]), n_arr, k, int(reorder),
+                    _ptr_array(ctypes.c_void_p, [ctypes.addressof(h) for h in hbufs]),
+                    _ptr_array(ctypes.c_int, [len(h) for h in heads]), chunk_bytes, sub_chunks,
+                    float(passthrough_threshold),
+                    _ptr_array(ctypes.c_void_p, [out.data_ptr() + o for o in offs]),
+                    _ptr_array(ctypes.c_int64, caps), sizes.data_ptr(), temp.data_ptr(), tb, stream,
+                ),
+                "zn_compress_batch",
+            )
+            pending.append((idx, out, offs, sizes, xs, temp))
+        all_sizes = torch.cat([p[3] for p in pending]).cpu().tolist()  # the one synchronization
+        pos = 0
+        for idx, out, offs, _, _, _ in pending:
+            for i, o in zip(idx, offs):
+                size = all_sizes[pos]
+                pos += 1
+                comp = out[o : o + size]
+                if readback_to_cpu:
+                    blob = _populated_empty(size, pin_memory=pin_memory)
+                    blob.copy_(comp, non_blocking=pin_memory)
+                    comp = blob
+                blobs[i] = comp
+        if readback_to_cpu and pin_memory:
+            torch.cuda.current_stream(device).synchronize()
+    return blobs  # type: ignore[return-value]
+
+
+def decompress_tensors(
+    blobs: list[torch.Tensor],
+    *,
+    compute_device: torch.device | str | None = None,
+    readback_to_cpu: bool = False,
+) -> list[torch.Tensor]:
+    """decompress_tensor over a list of blobs, with one kernel launch per stage for all blobs of an
+    element size.  Decoding errors are reported by last_decode_status()."""
+    compute_device = _check_device(compute_device)
+    outs: list[torch.Tensor | None] = [None] * len(blobs)
+    groups: dict[tuple[int, bool], list[tuple[int, tuple]]] = {}
+    for blob in blobs:
+        if blob.dtype != torch.uint8 or blob.dim() != 1:
+            raise ValueError("blob must be a 1-D uint8 tensor")
+    # Headers of GPU blobs come to the host in one copy per device.
+    plen = [min(b.numel(), _FIXED.size + 8 * _MAX_NDIM) for b in blobs]
+    prefixes: list[torch.Tensor | None] = [None] * len(blobs)
+    by_dev: dict[torch.device, list[int]] = {}
+    for i, b in enumerate(blobs):
+        if b.is_cuda:
+            by_dev.setdefault(b.device, []).append(i)
+        else:
+            prefixes[i] = b.detach()[: plen[i]].contiguous()
+    for idx in by_dev.values():
+        flat = torch.cat([blobs[i].detach()[: plen[i]] for i in idx]).cpu()
+        pos = 0
+        for i in idx:
+            prefixes[i] = flat[pos : pos + plen[i]]
+            pos += plen[i]
+    for i, blob in enumerate(blobs):
+        blob = blob.detach()
+        pre = prefixes[i]
+        dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(
+            (ctypes.c_byte * plen[i]).from_address(pre.data_ptr())
+        )
+        if flags & _FLAG_STORED or n == 0:
+            outs[i] = decompress_tensor(blob, compute_device=compute_device, readback_to_cpu=readback_to_cpu)
+            continue
+        if math.prod(shape) != n or chunk_bytes <= 0:
+            raise ValueError("not a cuzipnn blob")
+        k = dtype.itemsize
+        nch = -(-n // chunk_bytes)
+        _, _, data_off = _layout(len(shape), k * nch, n_comp)
+        if blob.numel() < data_off:
+            raise ValueError("blob is truncated")
+        groups.setdefault((k, bool(flags & _FLAG_REORDER)), []).append(
+            (i, (dtype, shape, chunk_bytes, n_comp, n))
+        )
+    if not groups:
+        return outs  # type: ignore[return-value]
+    first = blobs[next(iter(groups.values()))[0][0]]
+    device = _gpu(first, compute_device)
+    with torch.cuda.device(device):
+        stream = _stream(device)
+        uploaded = []
+        for (k, reorder), items in groups.items():
+            xs, ys, meta = [], [], []
+            for i, (dtype, shape, chunk_bytes, n_comp, n) in items:
+                x = blobs[i].detach().to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+                if x.data_ptr() % 8:
+                    x = x.clone()
+                if blobs[i].is_pinned():
+                    ev = torch.cuda.Event()
+                    ev.record()
+                    uploaded.append(ev)
+                xs.append(x)
+                y = torch.empty(shape, dtype=dtype, device=device)
+                ys.append(y)
+                meta.append((n, len(shape), chunk_bytes, n_comp))
+            nj = len(items)
+            n_arr = _ptr_array(ctypes.c_int64, [m[0] for m in meta])
+            c_arr = _ptr_array(ctypes.c_int64, [m[2] for m in meta])
+            tb = int(_lib.lib.zn_decompress_batch_temp_bytes(nj, n_arr, k, c_arr))
+            temp = torch.empty(max(tb, 1), dtype=torch.uint8, device=device)
+            status = torch.zeros(nj, dtype=torch.int32, device=device)
+            _lib.check(
+                _lib.lib.zn_decompress_batch(
+                    nj, _ptr_array(ctypes.c_void_p, [x.data_ptr() for x in xs]),
+                    _ptr_array(ctypes.c_int64, [x.numel() for x in xs]), n_arr, k, int(reorder),
+                    _ptr_array(ctypes.c_int, [m[1] for m in meta]), c_arr,
+                    _ptr_array(ctypes.c_int64, [m[3] for m in meta]),
+                    _ptr_array(ctypes.c_void_p, [y.data_ptr() for y in ys]), status.data_ptr(),
+                    temp.data_ptr(), tb, stream,
+                ),
+                "zn_decompress_batch",
+            )
+            _LAST_STATUS[device.index] = status
+            for (i, _), y in zip(items, ys):
+                outs[i] = y
+        for ev in uploaded:
+            ev.synchronize()
+        if readback_to_cpu:
+            for i, y in enumerate(outs):
+                if y is not None and y.is_cuda:
+                    host = _populated_empty(y.numel() * y.element_size()).view(y.dtype).view_as(y)
+                    host.copy_(y)
+                    outs[i] = host
+    return outs  # type: ignore[return-value]
 
 
 def _populated_empty(size: int, *, pin_memory: bool = False) -> torch.Tensor:

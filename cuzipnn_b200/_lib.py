@@ -28,6 +28,8 @@ SIGNATURES = {
     "zn_version": (_i32, []),
     "zn_last_error": (ctypes.c_char_p, []),
     "zn_launch_count": (ctypes.c_uint64, []),
+    "zn_timing_enable": (_i32, [ctypes.c_char_p, _i32]),
+    "zn_timing_read": (_i32, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
     "zn_split": (_i32, [_p, _i64, _i32, _i32, _p, _i64, _p]),
     "zn_merge": (_i32, [_p, _p, _p, _i64, _i32, _i64, _i32, _p]),
     "zn_copy_chunks": (_i32, [_p, _p, _p, _i64, _i64, _i32, _p]),
@@ -42,6 +44,10 @@ SIGNATURES = {
     "zn_compress_temp_bytes": (_sz, [_i64, _i32, _i64, _i32]),
     "zn_compress": (_i32, [_p, _i64, _i32, _i32, _p, _i32, _i64, _i32, ctypes.c_double, _p, _i64, _p, _p, _sz, _p]),
     "zn_decompress_temp_bytes": (_sz, [_i64, _i32, _i64]),
+    "zn_compress_batch_temp_bytes": (_sz, [_i32, _p, _i32, _i64, _i32]),
+    "zn_compress_batch": (_i32, [_i32, _p, _p, _i32, _i32, _p, _p, _i64, _i32, ctypes.c_double, _p, _p, _p, _p, _sz, _p]),
+    "zn_decompress_batch_temp_bytes": (_sz, [_i32, _p, _i32, _p]),
+    "zn_decompress_batch": (_i32, [_i32, _p, _p, _p, _i32, _i32, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "zn_decompress": (_i32, [_p, _i64, _i64, _i32, _i32, _i32, _i64, _i64, _p, _p, _p, _sz, _p]),
 }
 
@@ -78,3 +84,31 @@ def check(status: int, what: str) -> None:
 def launch_count() -> int:
     """Kernels launched by the library so far in this process."""
     return int(lib.zn_launch_count())
+
+
+KERNELS = ("hist", "encode", "scan", "pack", "dscan", "decode", "decode_overflow", "crc")
+
+
+class KernelTimer:
+    """CUDA-event timing of the library's kernel launches (zn_timing_enable), e.g.
+    `with KernelTimer() as kt: ...` then kt.times[name] = (total_ms, launches)."""
+
+    def __init__(self, kernel: str = "*"):
+        self.kernel = kernel
+        self.times: dict[str, tuple[float, int]] = {}
+
+    def __enter__(self):
+        lib.zn_timing_read(None, None, None)  # drop stale records
+        lib.zn_timing_enable(self.kernel.encode(), 1)
+        return self
+
+    def __exit__(self, *exc):
+        lib.zn_timing_enable(None, 0)
+        for name in KERNELS:
+            ms = ctypes.c_double()
+            n = ctypes.c_int64()
+            check(lib.zn_timing_read(name.encode(), ctypes.byref(ms), ctypes.byref(n)), "zn_timing_read")
+            if n.value:
+                self.times[name] = (ms.value, n.value)
+        lib.zn_timing_read(None, None, None)
+        return False

@@ -3,9 +3,12 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <set>
+#include <string>
 #include <utility>
+#include <vector>
 
 #include "zn_common.cuh"
 
@@ -44,9 +47,73 @@ int set_max_smem(const void* func, int bytes) {
   return ZN_OK;
 }
 
+// ---- opt-in kernel timing -----------------------------------------------------------------
+
+struct Timing {
+  std::mutex mu;
+  std::string kernel;  // "" = disabled, "*" = every kernel kind
+  struct Rec {
+    std::string kernel;
+    cudaEvent_t start, stop;
+  };
+  std::vector<Rec> pending;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pool;
+};
+static Timing g_timing;
+
+TimedLaunch::TimedLaunch(const char* kernel, cudaStream_t s) : slot(-1), stream(s) {
+  std::lock_guard<std::mutex> lock(g_timing.mu);
+  if (g_timing.kernel.empty() || (g_timing.kernel != "*" && g_timing.kernel != kernel)) return;
+  std::pair<cudaEvent_t, cudaEvent_t> ev;
+  if (!g_timing.pool.empty()) {
+    ev = g_timing.pool.back();
+    g_timing.pool.pop_back();
+  } else if (cudaEventCreate(&ev.first) != cudaSuccess || cudaEventCreate(&ev.second) != cudaSuccess) {
+    return;
+  }
+  cudaEventRecord(ev.first, s);
+  slot = int(g_timing.pending.size());
+  g_timing.pending.push_back({kernel, ev.first, ev.second});
+}
+
+TimedLaunch::~TimedLaunch() {
+  if (slot < 0) return;
+  std::lock_guard<std::mutex> lock(g_timing.mu);
+  if (slot < int(g_timing.pending.size())) cudaEventRecord(g_timing.pending[slot].stop, stream);
+}
+
 }  // namespace zn
 
 extern "C" {
+
+int zn_timing_enable(const char* kernel, int enable) {
+  std::lock_guard<std::mutex> lock(zn::g_timing.mu);
+  zn::g_timing.kernel = enable && kernel ? kernel : "";
+  return ZN_OK;
+}
+
+int zn_timing_read(const char* kernel, double* total_ms, int64_t* launches) {
+  std::lock_guard<std::mutex> lock(zn::g_timing.mu);
+  double sum = 0;
+  int64_t count = 0;
+  std::vector<zn::Timing::Rec> keep;
+  for (auto& r : zn::g_timing.pending) {
+    if (kernel && r.kernel != kernel) {
+      keep.push_back(r);
+      continue;
+    }
+    float ms = 0;
+    if (cudaEventSynchronize(r.stop) != cudaSuccess || cudaEventElapsedTime(&ms, r.start, r.stop) != cudaSuccess)
+      return zn::set_error(ZN_ERR_CUDA, "zn_timing_read: %s", cudaGetErrorString(cudaGetLastError()));
+    sum += ms;
+    ++count;
+    zn::g_timing.pool.push_back({r.start, r.stop});
+  }
+  zn::g_timing.pending.swap(keep);
+  if (launches) *launches = count;
+  if (total_ms) *total_ms = sum;
+  return ZN_OK;
+}
 
 int zn_version(void) { return ZN_ABI_VERSION; }
 const char* zn_last_error(void) { return zn::g_error; }

@@ -201,6 +201,35 @@ __device__ __forceinline__ void store_words(uint8_t* p, const uint32_t* w, int n
   }
 }
 
+// Index of the job whose chunk range holds global chunk `gchunk` (jobs sorted by chunk0; a job
+// without chunks never matches because the next job starts at the same chunk0).
+template <class J>
+__device__ __forceinline__ int find_job(const J* __restrict__ jobs, int njobs, int64_t gchunk) {
+  int lo = 0, hi = njobs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (jobs[mid].chunk0 <= gchunk) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Job tables reach device memory as kernel parameters (copied by the launch itself), so no host
+// staging buffer is needed: each launch carries up to ~30 KB of jobs.
+template <class T, int N>
+struct UploadBatch {
+  T items[N];
+  int count;
+};
+
+template <class T, int N>
+__global__ void upload_kernel(const __grid_constant__ UploadBatch<T, N> b, T* dst) {
+  static_assert(sizeof(T) % 4 == 0, "job size");
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(b.items);
+  uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+  for (int i = threadIdx.x; i < int(b.count * sizeof(T) / 4); i += blockDim.x) d[i] = src[i];
+}
+
 // ---- host side ------------------------------------------------------------------------------
 
 // Records the error of the last failing call of this thread and returns its status.
@@ -208,5 +237,29 @@ int set_error(int status, const char* fmt, ...);
 int check_launch(const char* what);
 void count_launch(int n = 1);
 int set_max_smem(const void* func, int bytes);
+
+// Copy `count` host structs to device memory at dev, on stream s, through kernel parameters.
+template <class T>
+int upload_jobs(const T* host, int count, T* dev, cudaStream_t s) {
+  constexpr int N = 30000 / int(sizeof(T)) > 0 ? 30000 / int(sizeof(T)) : 1;
+  for (int i = 0; i < count; i += N) {
+    UploadBatch<T, N> b;
+    b.count = count - i < N ? count - i : N;
+    for (int q = 0; q < b.count; ++q) b.items[q] = host[i + q];
+    upload_kernel<T, N><<<1, 256, 0, s>>>(b, dev + i);
+    count_launch();
+    if (int rc = check_launch("upload_kernel")) return rc;
+  }
+  return ZN_OK;
+}
+
+// Opt-in event timing of one kernel kind (zn_timing_enable): bracket a launch with
+// TimedLaunch t("decode", stream); ... launch ...; (the destructor records the end event).
+struct TimedLaunch {
+  TimedLaunch(const char* kernel, cudaStream_t stream);
+  ~TimedLaunch();
+  int slot;
+  cudaStream_t stream;
+};
 
 }  // namespace zn

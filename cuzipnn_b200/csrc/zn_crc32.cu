@@ -226,6 +226,7 @@ int zn_crc32(const void* data, int64_t nbytes, int64_t segment_bytes, uint32_t* 
     const int64_t groups = kThreads / G;
     const int64_t grid = cdiv(nseg, groups);
     if (grid > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_crc32: too many segments");
+    TimedLaunch tl("crc", st);
     crc_level1<<<unsigned(grid), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, G, 1, true, out, nullptr);
     count_launch();
     return check_launch("zn_crc32");

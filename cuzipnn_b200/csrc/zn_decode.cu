@@ -13,6 +13,8 @@
 // Every blob access is bounds-checked; a malformed unit raises a bit in the status word and its
 // elements are zeroed.  No wait in these kernels depends on another thread's progress except
 // __syncthreads().
+#include <vector>
+
 #include "zn_common.cuh"
 
 namespace zn {
@@ -24,13 +26,15 @@ constexpr int kSym = 256 / kDecThreads;  // symbols per thread in table building
 constexpr int64_t kCodedBit = int64_t(1) << 62;
 constexpr int64_t kOffMask = kCodedBit - 1;
 
+// One decompression job (a blob, or the payload list of the batched seam).  Jobs live in device
+// memory; a decode CTA finds its job by global chunk index (find_job).
 struct DecArgs {
-  // fused mode
+  // whole-blob mode
   const uint8_t* blob;
   int64_t blob_bytes;
-  const int64_t* src;     // per unit: blob offset | kCodedBit, or -1 if invalid
-  int64_t sizes_off;
-  int64_t n, C, nch;
+  int64_t* src;           // per unit: blob offset | kCodedBit, or -1 if invalid
+  int64_t sizes_off, idx_off, data_off, n_comp;
+  int64_t n, C, nch, units, chunk0;
   uint8_t* out;
   int32_t* status;
   // batched mode (K == 1): payload i at in_ptrs[i] (in_bytes[i]) decodes into out_ptrs[i]
@@ -254,14 +258,15 @@ __device__ __forceinline__ void decode_round(Cursor* cb, const uint32_t* __restr
 // Work split: a warp item is 8 sub-chunks; lane l of 8-lane segment g runs chain c on sub-chunk
 // 8 * item + 4 * c + g.
 template <int K, bool REORDER, int KC>
-__global__ void __launch_bounds__(kDecThreads) decode_kernel(DecArgs a, bool overflow_pass) {
+__global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __restrict__ jobs, int njobs, bool overflow_pass) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   constexpr int RH = ring_half<KC>();
   uint32_t* tabs = reinterpret_cast<uint32_t*>(smem_raw);                      // [KC][4096]
   uint4* rings = reinterpret_cast<uint4*>(smem_raw + KC * kM * 4);             // [KC][kChains][threads][RH / 8]
   DecSmem& S = *reinterpret_cast<DecSmem*>(smem_raw + KC * kM * 4 + KC * kChains * kDecThreads * RH * 2);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t j = blockIdx.x;
+  const DecArgs& a = jobs[find_job(jobs, njobs, blockIdx.x)];
+  const int64_t j = blockIdx.x - a.chunk0;
   if (overflow_pass && !a.overflow[j]) return;
   const bool batched = a.in_ptrs != nullptr;
   int64_t m;
@@ -506,26 +511,19 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(DecArgs a, bool ove
 
 constexpr int kScanThreads = 1024;
 
-struct DScanArgs {
-  const uint8_t* blob;
-  int64_t blob_bytes;
-  int64_t total, nch, C, n;
-  int64_t sizes_off, idx_off, n_comp, data_off;
-  int64_t* src;
-  int32_t* status;
-};
-
-__global__ void __launch_bounds__(kScanThreads) dscan_kernel(DScanArgs a) {
+// One CTA per job.
+__global__ void __launch_bounds__(kScanThreads) dscan_kernel(const DecArgs* __restrict__ jobs) {
   __shared__ int64_t sm[64];
+  const DecArgs& a = jobs[blockIdx.x];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int64_t last = a.n - (a.nch - 1) * a.C;
   const int32_t* stored = reinterpret_cast<const int32_t*>(a.blob + a.sizes_off);
   int64_t carry = a.data_off;
   bool bad = false;
-  for (int64_t start = 0; start < a.total; start += kScanThreads) {
+  for (int64_t start = 0; start < a.units; start += kScanThreads) {
     const int64_t i = start + tid;
     int64_t v = 0;
-    if (i < a.total) {
+    if (i < a.units) {
       const int64_t s = stored[i];
       bad |= s < 0;
       v = s < 0 ? 0 : align8(s);
@@ -547,7 +545,7 @@ __global__ void __launch_bounds__(kScanThreads) dscan_kernel(DScanArgs a) {
     }
     __syncthreads();
     const int64_t excl = carry + (w ? sm[32 + w - 1] : 0) + incl - v;
-    if (i < a.total) a.src[i] = excl;
+    if (i < a.units) a.src[i] = excl;
     carry += sm[32 + 31];
     __syncthreads();
   }
@@ -555,11 +553,11 @@ __global__ void __launch_bounds__(kScanThreads) dscan_kernel(DScanArgs a) {
   const int32_t* idx = reinterpret_cast<const int32_t*>(a.blob + a.idx_off);
   for (int64_t q = tid; q < a.n_comp; q += kScanThreads) {
     const int64_t i = idx[q];
-    if (i < 0 || i >= a.total) { bad = true; continue; }
+    if (i < 0 || i >= a.units) { bad = true; continue; }
     a.src[i] |= kCodedBit;
   }
   __syncthreads();
-  for (int64_t i = tid; i < a.total; i += kScanThreads) {
+  for (int64_t i = tid; i < a.units; i += kScanThreads) {
     const int64_t s = a.src[i];
     const int64_t off = s & kOffMask, st = stored[i];
     const int64_t raw = (i % a.nch) == a.nch - 1 ? last : a.C;
@@ -578,21 +576,31 @@ size_t dec_smem(int KC) {
 }
 
 template <int K, bool REORDER, int KC>
-int launch_decode_pass(const DecArgs& a, int64_t grid, bool overflow_pass, cudaStream_t s) {
+int launch_decode_pass(const DecArgs* jobs, int njobs, int64_t grid, bool overflow_pass, cudaStream_t s) {
   const size_t sm = dec_smem(KC);
   auto fn = decode_kernel<K, REORDER, KC>;
   if (int rc = set_max_smem(reinterpret_cast<const void*>(fn), int(sm))) return rc;
-  fn<<<unsigned(grid), kDecThreads, sm, s>>>(a, overflow_pass);
+  {
+    TimedLaunch tl(overflow_pass ? "decode_overflow" : "decode", s);
+    fn<<<unsigned(grid), kDecThreads, sm, s>>>(jobs, njobs, overflow_pass);
+  }
   count_launch();
   return check_launch("decode_kernel");
 }
 
 // Main pass with one coded plane per chunk in shared memory, then (K > 1) the overflow pass.
 template <int K, bool REORDER>
-int launch_decode(const DecArgs& a, int64_t grid, cudaStream_t s) {
-  if (int rc = launch_decode_pass<K, REORDER, 1>(a, grid, false, s)) return rc;
-  if constexpr (K > 1) return launch_decode_pass<K, REORDER, K>(a, grid, true, s);
+int launch_decode(const DecArgs* jobs, int njobs, int64_t grid, cudaStream_t s) {
+  if (grid <= 0) return ZN_OK;
+  if (int rc = launch_decode_pass<K, REORDER, 1>(jobs, njobs, grid, false, s)) return rc;
+  if constexpr (K > 1) return launch_decode_pass<K, REORDER, K>(jobs, njobs, grid, true, s);
   return ZN_OK;
+}
+
+size_t dec_table_bytes(int njobs) { return (size_t(njobs) * sizeof(DecArgs) + 255) & ~size_t(255); }
+size_t dec_job_bytes(int64_t n, int k, int64_t chunk_bytes) {
+  const int64_t nch = cdiv(n, chunk_bytes);
+  return (size_t(int64_t(k) * nch) * 8 + size_t(nch) + 255) & ~size_t(255);  // unit offsets, overflow flags
 }
 
 }  // namespace
@@ -602,14 +610,14 @@ using namespace zn;
 
 extern "C" {
 
-size_t zn_ans_decompress_temp_bytes(int64_t count) { (void)count; return 0; }
+size_t zn_ans_decompress_temp_bytes(int64_t count) { (void)count; return dec_table_bytes(1); }
 
 int zn_ans_decompress(const int64_t* in_ptrs, const int64_t* in_bytes, const int64_t* out_capacity, int64_t count,
                       const int64_t* out_ptrs, int32_t* statuses, void* temp, size_t temp_bytes, void* stream) {
-  (void)temp;
-  (void)temp_bytes;
   if (count < 0 || count > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_ans_decompress: bad arguments");
   if (count == 0) return ZN_OK;
+  if (!temp || temp_bytes < dec_table_bytes(1)) return set_error(ZN_ERR_SPACE, "zn_ans_decompress: temp buffer too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   DecArgs a{};
   a.in_ptrs = in_ptrs;
   a.in_bytes = in_bytes;
@@ -617,64 +625,91 @@ int zn_ans_decompress(const int64_t* in_ptrs, const int64_t* in_bytes, const int
   a.out_cap = out_capacity;
   a.statuses = statuses;
   a.nch = count;
-  return launch_decode<1, false>(a, count, static_cast<cudaStream_t>(stream));
+  DecArgs* dj = static_cast<DecArgs*>(temp);
+  if (int rc = upload_jobs(&a, 1, dj, s)) return rc;
+  return launch_decode<1, false>(dj, 1, count, s);
+}
+
+size_t zn_decompress_batch_temp_bytes(int njobs, const int64_t* n, int k, const int64_t* chunk_bytes) {
+  if (njobs < 0 || k <= 0) return 0;
+  size_t total = dec_table_bytes(njobs);
+  for (int i = 0; i < njobs; ++i) {
+    if (n[i] < 0 || chunk_bytes[i] <= 0) return 0;
+    total += dec_job_bytes(n[i], k, chunk_bytes[i]);
+  }
+  return total;
 }
 
 size_t zn_decompress_temp_bytes(int64_t n, int k, int64_t chunk_bytes) {
-  if (n < 0 || k <= 0 || chunk_bytes <= 0) return 0;
-  const int64_t nch = cdiv(n, chunk_bytes);
-  return size_t(int64_t(k) * nch) * 8 + size_t(nch);  // unit offsets, then per-chunk overflow flags
+  return zn_decompress_batch_temp_bytes(1, &n, k, &chunk_bytes);
+}
+
+int zn_decompress_batch(int njobs, const void* const* blobs, const int64_t* blob_bytes, const int64_t* n, int k,
+                        int reorder, const int* ndim, const int64_t* chunk_bytes, const int64_t* n_comp,
+                        void* const* out, int32_t* status, void* temp, size_t temp_bytes, void* stream) {
+  if (njobs < 0 || (k != 1 && k != 2 && k != 4 && k != 8) || (reorder && k != 2 && k != 4))
+    return set_error(ZN_ERR_INVALID, "zn_decompress: bad arguments");
+  if (njobs == 0) return ZN_OK;
+  if (!temp || temp_bytes < zn_decompress_batch_temp_bytes(njobs, n, k, chunk_bytes))
+    return set_error(ZN_ERR_SPACE, "zn_decompress: temp buffer too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* tb = static_cast<uint8_t*>(temp);
+  uint8_t* region = tb + dec_table_bytes(njobs);
+  std::vector<DecArgs> jobs;
+  jobs.reserve(static_cast<size_t>(njobs));
+  int64_t chunk0 = 0;
+  for (int i = 0; i < njobs; ++i) {
+    if (n[i] < 0 || chunk_bytes[i] <= 0 || ndim[i] < 0 || ndim[i] > 64 || n_comp[i] < 0 ||
+        (reinterpret_cast<uintptr_t>(blobs[i]) & 7))
+      return set_error(ZN_ERR_INVALID, "zn_decompress: bad arguments (job %d)", i);
+    if (n[i] == 0) continue;
+    DecArgs a{};
+    a.blob = static_cast<const uint8_t*>(blobs[i]);
+    a.blob_bytes = blob_bytes[i];
+    a.n = n[i];
+    a.C = chunk_bytes[i];
+    a.nch = cdiv(n[i], chunk_bytes[i]);
+    a.units = int64_t(k) * a.nch;
+    if (a.nch > 0x7FFFFFFF || n_comp[i] > a.units) return set_error(ZN_ERR_INVALID, "zn_decompress: bad tables (job %d)", i);
+    a.sizes_off = 24 + 8 * int64_t(ndim[i]);
+    a.idx_off = a.sizes_off + 4 * a.units;
+    a.n_comp = n_comp[i];
+    a.data_off = align8(a.idx_off + 4 * a.n_comp);
+    if (a.blob_bytes < a.data_off) return set_error(ZN_ERR_INVALID, "zn_decompress: blob is truncated (job %d)", i);
+    a.chunk0 = chunk0;
+    a.out = static_cast<uint8_t*>(out[i]);
+    a.status = status + i;
+    a.src = reinterpret_cast<int64_t*>(region);
+    a.overflow = region + size_t(a.units) * 8;
+    region += dec_job_bytes(n[i], k, chunk_bytes[i]);
+    chunk0 += a.nch;
+    jobs.push_back(a);
+  }
+  const int nj = int(jobs.size());
+  if (nj == 0) return ZN_OK;
+  if (chunk0 > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_decompress: too many chunks");
+  DecArgs* dj = reinterpret_cast<DecArgs*>(tb);
+  if (int rc = upload_jobs(jobs.data(), nj, dj, s)) return rc;
+  {
+    TimedLaunch tl("dscan", s);
+    dscan_kernel<<<unsigned(nj), kScanThreads, 0, s>>>(dj);
+  }
+  count_launch();
+  if (int rc = check_launch("dscan_kernel")) return rc;
+  switch (k * 2 + (reorder ? 1 : 0)) {
+    case 2: return launch_decode<1, false>(dj, nj, chunk0, s);
+    case 4: return launch_decode<2, false>(dj, nj, chunk0, s);
+    case 5: return launch_decode<2, true>(dj, nj, chunk0, s);
+    case 8: return launch_decode<4, false>(dj, nj, chunk0, s);
+    case 9: return launch_decode<4, true>(dj, nj, chunk0, s);
+    default: return launch_decode<8, false>(dj, nj, chunk0, s);
+  }
 }
 
 int zn_decompress(const void* blob, int64_t blob_bytes, int64_t n, int k, int reorder, int ndim, int64_t chunk_bytes,
                   int64_t n_comp, void* out, int32_t* status, void* temp, size_t temp_bytes, void* stream) {
-  if (n < 0 || (k != 1 && k != 2 && k != 4 && k != 8) || (reorder && k != 2 && k != 4) || chunk_bytes <= 0 ||
-      ndim < 0 || ndim > 64 || n_comp < 0 || (reinterpret_cast<uintptr_t>(blob) & 7))
-    return set_error(ZN_ERR_INVALID, "zn_decompress: bad arguments");
-  if (n == 0) return ZN_OK;
-  const int64_t nch = cdiv(n, chunk_bytes), total = int64_t(k) * nch;
-  if (nch > 0x7FFFFFFF || n_comp > total) return set_error(ZN_ERR_INVALID, "zn_decompress: bad tables");
-  const int64_t sizes_off = 24 + 8 * int64_t(ndim), idx_off = sizes_off + 4 * total;
-  const int64_t data_off = align8(idx_off + 4 * n_comp);
-  if (blob_bytes < data_off) return set_error(ZN_ERR_INVALID, "zn_decompress: blob is truncated");
-  if (!temp || temp_bytes < size_t(total) * 8 + size_t(nch))
-    return set_error(ZN_ERR_SPACE, "zn_decompress: temp buffer too small");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  DScanArgs sa{};
-  sa.blob = static_cast<const uint8_t*>(blob);
-  sa.blob_bytes = blob_bytes;
-  sa.total = total;
-  sa.nch = nch;
-  sa.C = chunk_bytes;
-  sa.n = n;
-  sa.sizes_off = sizes_off;
-  sa.idx_off = idx_off;
-  sa.n_comp = n_comp;
-  sa.data_off = data_off;
-  sa.src = static_cast<int64_t*>(temp);
-  sa.status = status;
-  dscan_kernel<<<1, kScanThreads, 0, s>>>(sa);
-  count_launch();
-  if (int rc = check_launch("dscan_kernel")) return rc;
-  DecArgs a{};
-  a.blob = sa.blob;
-  a.blob_bytes = blob_bytes;
-  a.src = sa.src;
-  a.sizes_off = sizes_off;
-  a.n = n;
-  a.C = chunk_bytes;
-  a.nch = nch;
-  a.out = static_cast<uint8_t*>(out);
-  a.status = status;
-  a.overflow = static_cast<uint8_t*>(temp) + size_t(total) * 8;
-  switch (k * 2 + (reorder ? 1 : 0)) {
-    case 2: return launch_decode<1, false>(a, nch, s);
-    case 4: return launch_decode<2, false>(a, nch, s);
-    case 5: return launch_decode<2, true>(a, nch, s);
-    case 8: return launch_decode<4, false>(a, nch, s);
-    case 9: return launch_decode<4, true>(a, nch, s);
-    default: return launch_decode<8, false>(a, nch, s);
-  }
+  return zn_decompress_batch(1, &blob, &blob_bytes, &n, k, reorder, &ndim, &chunk_bytes, &n_comp, &out, status, temp,
+                             temp_bytes, stream);
 }
 
 }  // extern "C"

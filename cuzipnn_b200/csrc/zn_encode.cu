@@ -15,6 +15,9 @@
 //      encoded chunks are still in L2), writes raw planes straight from the elements and copies
 //      the coded payloads from scratch, zero-padding every unit to 8 bytes.
 #include <math.h>
+#include <string.h>
+
+#include <vector>
 
 #include "zn_common.cuh"
 
@@ -27,16 +30,20 @@ constexpr int kEncChains = 1;  // rANS states per lane (sub-chunks per lane)
 static_assert(kEncChains == 1, "the staging ring holds one state per lane");
 constexpr int kCols = 16;  // lane-private histogram columns
 
+// One compression job (a tensor, or the chunk list of the batched seam).  Jobs live in device
+// memory; a kernel's CTA finds its job by global chunk index (find_job).
 struct EncArgs {
-  const uint8_t* x;         // fused: tensor elements
-  const int64_t* in_ptrs;   // batched: chunk addresses (K == 1), else null
-  const int64_t* in_bytes;  // batched: chunk sizes
-  int64_t n;                // fused: element count
+  const uint8_t* x;         // tensor elements
+  const int64_t* in_ptrs;   // seam: chunk addresses (K == 1), else null
+  const int64_t* in_bytes;  // seam: chunk sizes
+  int64_t n;                // element count
   int64_t C;                // elements per chunk
   int64_t nch;              // chunks (units per plane)
+  int64_t units;            // K * nch
+  int64_t chunk0;           // global index of the job's first chunk
   int t;                    // log2(sub-chunks)
-  double threshold;         // passthrough threshold (batched: skipping disabled)
-  bool allow_skip;
+  int allow_skip;           // seam: 0 (every chunk is coded)
+  double threshold;         // passthrough threshold
   uint8_t* meta;            // per unit, meta_slot bytes
   int64_t meta_slot;
   uint16_t* streams;        // per unit: unit_words words; per sub-chunk: sub_words; per lane: lane_words
@@ -44,7 +51,14 @@ struct EncArgs {
   int64_t sub_words;
   int64_t lane_words;
   int32_t* comp_bytes;      // per unit: payload bytes, or -1 if not coded
-  const uint32_t* part_hist;  // [nch][kHistParts][K][256] partial histograms from hist_kernel
+  uint32_t* part_hist;      // [nch][kHistParts][K][256] partial histograms from hist_kernel
+  int64_t* dst_rel;         // per unit: offset from data_off, with bit 62 set if coded
+  int64_t* scalars;         // [0] = data_off, [1] = size
+  uint8_t* out;             // blob buffer
+  uint64_t* size_out;       // device u64 receiving the blob size
+  int64_t sizes_off, idx_off;
+  int header_len;
+  uint8_t header[24 + 8 * 64];
 };
 
 // Parts per chunk of the histogram kernel: a chunk's histogram is built by kHistParts CTAs, so
@@ -197,10 +211,11 @@ __device__ __forceinline__ int64_t hist_vectors(const uint8_t* xc, int64_t m, ui
 // Part `blockIdx.y` of chunk `blockIdx.x`: histograms of all K planes of its elements, written as
 // one partial histogram per plane (no global atomics; the encoder sums the parts).
 template <int K, bool REORDER>
-__global__ void __launch_bounds__(kHistThreads) hist_kernel(EncArgs a) {
+__global__ void __launch_bounds__(kHistThreads) hist_kernel(const EncArgs* __restrict__ jobs, int njobs) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem_raw);  // [K][256][kCols]
-  const int64_t j = blockIdx.x;
+  const EncArgs& a = jobs[find_job(jobs, njobs, blockIdx.x)];
+  const int64_t j = blockIdx.x - a.chunk0;
   const int part = blockIdx.y, tid = threadIdx.x;
   const uint8_t* xc;
   int64_t m;
@@ -230,7 +245,7 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(EncArgs a) {
     for (int b = 0; b < K; ++b) atomicAdd(&hist[((b << 8) | uint32_t((u >> (8 * b)) & 0xFF)) * kCols + col], 1u);
   }
   __syncthreads();
-  uint32_t* outp = const_cast<uint32_t*>(a.part_hist) + (j * kHistParts + part) * K * 256;
+  uint32_t* outp = a.part_hist + (j * kHistParts + part) * K * 256;
   for (int i = tid; i < K * 256; i += kHistThreads) {
     uint32_t c = 0;
 #pragma unroll
@@ -272,12 +287,12 @@ __device__ __forceinline__ void encode_round(uint32_t* x, uint32_t* wp, uint16_t
 // ---- the encoder ----------------------------------------------------------------------------
 
 template <int K, bool REORDER>
-__global__ void __launch_bounds__(kEncThreads) encode_kernel(EncArgs a) {
+__global__ void __launch_bounds__(kEncThreads) encode_kernel(const EncArgs* __restrict__ jobs, int njobs) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint4* etab = reinterpret_cast<uint4*>(smem_raw);                         // [K][256]
   EncSmem& S = *reinterpret_cast<EncSmem*>(smem_raw + K * 256 * 16);
-
-  const int64_t j = blockIdx.x;
+  const EncArgs& a = jobs[find_job(jobs, njobs, blockIdx.x)];
+  const int64_t j = blockIdx.x - a.chunk0;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint8_t* xc;
   int64_t m;
@@ -554,23 +569,6 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(EncArgs a) {
 constexpr int kScanThreads = 1024;
 constexpr int kScanPer = 4;
 
-struct HeaderParam {
-  uint8_t bytes[24 + 8 * 64];
-  int len;
-};
-
-struct ScanArgs {
-  const int32_t* comp_bytes;
-  int64_t total, nch, C, n;
-  double threshold;
-  int64_t sizes_off, idx_off;
-  uint8_t* out;
-  int64_t* dst_rel;      // per unit: offset from data_off, with bit 62 set if coded
-  int64_t* scalars;      // [0] = data_off, [1] = size
-  uint64_t* size_out;
-  HeaderParam header;
-};
-
 __device__ __forceinline__ void block_scan2(int64_t& a, int64_t& b, int64_t& ta, int64_t& tb, int64_t* sm) {
   // Exclusive scan of (a, b) over kScanThreads threads; totals returned in ta, tb.
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -599,12 +597,14 @@ __device__ __forceinline__ void block_scan2(int64_t& a, int64_t& b, int64_t& ta,
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
+// One CTA per job.
+__global__ void __launch_bounds__(kScanThreads) scan_kernel(const EncArgs* __restrict__ jobs) {
   __shared__ int64_t sm[128];
+  const EncArgs& a = jobs[blockIdx.x];
   const int tid = threadIdx.x;
   const int64_t last = a.n - (a.nch - 1) * a.C;
   int64_t carry_data = 0, carry_comp = 0;
-  for (int64_t start = 0; start < a.total; start += int64_t(kScanThreads) * kScanPer) {
+  for (int64_t start = 0; start < a.units; start += int64_t(kScanThreads) * kScanPer) {
     int64_t stored[kScanPer];
     bool use[kScanPer];
     int64_t sd = 0, sc = 0;
@@ -613,7 +613,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
       const int64_t i = start + int64_t(tid) * kScanPer + q;
       use[q] = false;
       stored[q] = 0;
-      if (i < a.total) {
+      if (i < a.units) {
         const int64_t jj = i % a.nch;
         const int64_t raw = jj == a.nch - 1 ? last : a.C;
         const int64_t thr = __double2ll_rz(double(raw) * a.threshold);
@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
 #pragma unroll
     for (int q = 0; q < kScanPer; ++q) {
       const int64_t i = start + int64_t(tid) * kScanPer + q;
-      if (i < a.total) {
+      if (i < a.units) {
         a.dst_rel[i] = (carry_data + sd) | (int64_t(use[q]) << 62);
         if (use[q]) *reinterpret_cast<int32_t*>(a.out + a.idx_off + 4 * (carry_comp + sc)) = int32_t(i);
         sd += align8(stored[q]);
@@ -643,8 +643,8 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
   const int64_t n_comp = carry_comp;
   const int64_t data_off = align8(a.idx_off + 4 * n_comp);
   const int64_t size = data_off + carry_data;
-  for (int i = tid; i < a.header.len; i += kScanThreads) {
-    uint8_t v = a.header.bytes[i];
+  for (int i = tid; i < a.header_len; i += kScanThreads) {
+    uint8_t v = a.header[i];
     if (i >= 12 && i < 16) v = uint8_t(uint64_t(n_comp) >> (8 * (i - 12)));
     a.out[i] = v;
   }
@@ -659,20 +659,6 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
 // ---- pack (src/cuzipnn/_codec.py:381-403) ---------------------------------------------------
 
 constexpr int kPackThreads = 256;
-
-struct PackArgs {
-  const uint8_t* x;
-  int64_t n, C, nch;
-  const int32_t* comp_bytes;
-  const int64_t* dst_rel;
-  const int64_t* scalars;
-  const uint8_t* meta;
-  int64_t meta_slot;
-  const uint16_t* streams;
-  int64_t unit_words, sub_words, lane_words;
-  int t;
-  uint8_t* out;
-};
 
 __device__ __forceinline__ int count_present(const uint8_t* meta) {
   int np = 0;
@@ -732,7 +718,7 @@ __device__ void stream_prefix(const uint8_t* meta, int64_t tb, const Geom& g, in
 // Copy part `part` of `nparts` of one coded payload to dst (2-byte aligned): the meta block (part
 // 0), then its share of the nu * 8 streams, each from the tail of its slot, one warp per stream.
 // Called by all threads of the CTA.
-__device__ void copy_payload(const PackArgs& a, uint64_t u, int64_t m, uint8_t* dst, int npres, int part, int nparts,
+__device__ void copy_payload(const EncArgs& a, uint64_t u, int64_t m, uint8_t* dst, int npres, int part, int nparts,
                              int32_t* pre, int32_t* warp_tot) {
   const uint8_t* meta = a.meta + u * a.meta_slot;
   const Geom g = geom_of(m, a.t);
@@ -763,10 +749,12 @@ __device__ void copy_payload(const PackArgs& a, uint64_t u, int64_t m, uint8_t* 
 constexpr int kPackParts = 8;
 
 template <int K, bool REORDER>
-__global__ void __launch_bounds__(kPackThreads) pack_kernel(PackArgs a) {
+__global__ void __launch_bounds__(kPackThreads) pack_kernel(const EncArgs* __restrict__ jobs, int njobs, int64_t total_chunks) {
   __shared__ int32_t pre[512];
   __shared__ int32_t warp_tot[kPackThreads / 32];
-  const int64_t j = a.nch - 1 - blockIdx.x;
+  const int64_t gj = total_chunks - 1 - blockIdx.x;
+  const EncArgs& a = jobs[find_job(jobs, njobs, gj)];
+  const int64_t j = gj - a.chunk0;
   const int part = blockIdx.y;
   const int64_t m = min(a.C, a.n - j * a.C);
   const int64_t data_off = a.scalars[0];
@@ -841,9 +829,10 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(PackArgs a) {
 
 // ---- batched seam: assemble each payload into the caller's out_ptrs[i] ---------------------
 
-__global__ void __launch_bounds__(kPackThreads) assemble_kernel(PackArgs a, const int64_t* in_bytes,
+__global__ void __launch_bounds__(kPackThreads) assemble_kernel(const EncArgs* __restrict__ job, const int64_t* in_bytes,
                                                                 const int64_t* out_ptrs, int64_t* out_bytes,
                                                                 int32_t* statuses) {
+  const EncArgs& a = *job;
   const int64_t i = blockIdx.x;
   const int64_t size = a.comp_bytes[i];
   if (size < 0) {
@@ -866,6 +855,7 @@ struct EncLayout {
   size_t off_comp, off_dst, off_scalars, off_hist, off_meta, off_streams, total;
 };
 
+// Scratch of one job with `units` (plane, chunk) units of chunk length C and 2^t sub-chunks.
 EncLayout enc_layout(int64_t units, int64_t C, int t) {
   EncLayout L;
   // A shorter last unit can have more (smaller) sub-chunks than a full one, so the slots are
@@ -880,7 +870,7 @@ EncLayout enc_layout(int64_t units, int64_t C, int t) {
   L.off_comp = take(size_t(units) * 4);
   L.off_dst = take(size_t(units) * 8);
   L.off_scalars = take(64);
-  L.off_hist = take(size_t(units) * kHistParts * 256 * 4);  // units = K * nch
+  L.off_hist = take(size_t(units) * kHistParts * 256 * 4);
   L.off_meta = take(size_t(units) * size_t(L.meta_slot));
   L.off_streams = take(size_t(units) * size_t(L.unit_words) * 2);
   L.total = o;
@@ -890,31 +880,59 @@ EncLayout enc_layout(int64_t units, int64_t C, int t) {
 size_t enc_smem(int K) { return size_t(K) * 256 * 16 + sizeof(EncSmem); }
 size_t hist_smem(int K) { return size_t(K) * 256 * kCols * 4; }
 
-template <int K, bool REORDER>
-int launch_encode(const EncArgs& a, int64_t grid, cudaStream_t s) {
-  const size_t hs = hist_smem(K);
-  auto hf = hist_kernel<K, REORDER>;
-  if (int rc = set_max_smem(reinterpret_cast<const void*>(hf), int(hs))) return rc;
-  hf<<<dim3(unsigned(grid), kHistParts), kHistThreads, hs, s>>>(a);
-  const size_t sm = enc_smem(K);
-  auto fn = encode_kernel<K, REORDER>;
-  if (int rc = set_max_smem(reinterpret_cast<const void*>(fn), int(sm))) return rc;
-  fn<<<unsigned(grid), kEncThreads, sm, s>>>(a);
-  count_launch(2);
-  return check_launch("encode_kernel");
-}
-
-template <int K, bool REORDER>
-void launch_pack(const PackArgs& p, int64_t grid, cudaStream_t s) {
-  pack_kernel<K, REORDER><<<dim3(unsigned(grid), kPackParts), kPackThreads, 0, s>>>(p);
-  count_launch();
-}
+size_t job_table_bytes(int njobs) { return (size_t(njobs) * sizeof(EncArgs) + 255) & ~size_t(255); }
 
 int sub_log2(int sub_chunks) {
   for (int t = kMinSubLog2; t <= kMaxSubLog2; ++t)
     if (sub_chunks == (1 << t)) return t;
   return -1;
 }
+
+// Point a job's scratch pointers at its region of the temp buffer.
+void bind_scratch(EncArgs& a, uint8_t* region, int64_t units) {
+  const EncLayout L = enc_layout(units, a.C, a.t);
+  a.meta = region + L.off_meta;
+  a.meta_slot = L.meta_slot;
+  a.streams = reinterpret_cast<uint16_t*>(region + L.off_streams);
+  a.unit_words = L.unit_words;
+  a.sub_words = L.sub_words;
+  a.lane_words = L.lane_words;
+  a.comp_bytes = reinterpret_cast<int32_t*>(region + L.off_comp);
+  a.part_hist = reinterpret_cast<uint32_t*>(region + L.off_hist);
+  a.dst_rel = reinterpret_cast<int64_t*>(region + L.off_dst);
+  a.scalars = reinterpret_cast<int64_t*>(region + L.off_scalars);
+}
+
+template <int K, bool REORDER>
+int launch_encode(const EncArgs* jobs, int njobs, int64_t grid, cudaStream_t s) {
+  if (grid <= 0) return ZN_OK;
+  const size_t hs = hist_smem(K);
+  auto hf = hist_kernel<K, REORDER>;
+  if (int rc = set_max_smem(reinterpret_cast<const void*>(hf), int(hs))) return rc;
+  {
+    TimedLaunch tl("hist", s);
+    hf<<<dim3(unsigned(grid), kHistParts), kHistThreads, hs, s>>>(jobs, njobs);
+  }
+  const size_t sm = enc_smem(K);
+  auto fn = encode_kernel<K, REORDER>;
+  if (int rc = set_max_smem(reinterpret_cast<const void*>(fn), int(sm))) return rc;
+  {
+    TimedLaunch tl("encode", s);
+    fn<<<unsigned(grid), kEncThreads, sm, s>>>(jobs, njobs);
+  }
+  count_launch(2);
+  return check_launch("encode_kernel");
+}
+
+template <int K, bool REORDER>
+void launch_pack(const EncArgs* jobs, int njobs, int64_t grid, cudaStream_t s) {
+  if (grid <= 0) return;
+  TimedLaunch tl("pack", s);
+  pack_kernel<K, REORDER><<<dim3(unsigned(grid), kPackParts), kPackThreads, 0, s>>>(jobs, njobs, grid);
+  count_launch();
+}
+
+bool valid_k(int k, int reorder) { return (k == 1 || k == 2 || k == 4 || k == 8) && !(reorder && k != 2 && k != 4); }
 
 }  // namespace
 }  // namespace zn
@@ -932,7 +950,7 @@ int64_t zn_ans_max_compressed_chunk_bytes(int64_t chunk_bytes, int sub_chunks) {
 size_t zn_ans_compress_temp_bytes(int64_t count, int64_t chunk_bytes, int sub_chunks) {
   const int t = sub_log2(sub_chunks);
   if (t < 0 || count < 0 || chunk_bytes <= 0) return 0;
-  return enc_layout(count, chunk_bytes, t).total;
+  return job_table_bytes(1) + enc_layout(count, chunk_bytes, t).total;
 }
 
 int zn_ans_compress(const int64_t* in_ptrs, const int64_t* in_bytes, int64_t chunk_bytes, int64_t count,
@@ -942,39 +960,23 @@ int zn_ans_compress(const int64_t* in_ptrs, const int64_t* in_bytes, int64_t chu
   if (t < 0 || count < 0 || count > 0x7FFFFFFF || chunk_bytes <= 0 || chunk_bytes > kMaxChunkBytes)
     return set_error(ZN_ERR_INVALID, "zn_ans_compress: bad arguments");
   if (count == 0) return ZN_OK;
-  const EncLayout L = enc_layout(count, chunk_bytes, t);
-  if (!temp || temp_bytes < L.total) return set_error(ZN_ERR_SPACE, "zn_ans_compress: temp buffer too small");
+  if (!temp || temp_bytes < zn_ans_compress_temp_bytes(count, chunk_bytes, sub_chunks))
+    return set_error(ZN_ERR_SPACE, "zn_ans_compress: temp buffer too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* tb = static_cast<uint8_t*>(temp);
   EncArgs a{};
   a.in_ptrs = in_ptrs;
   a.in_bytes = in_bytes;
   a.C = chunk_bytes;
-  a.nch = count;
+  a.nch = a.units = count;
   a.t = t;
-  a.allow_skip = false;
+  a.allow_skip = 0;
   a.threshold = 1.0;
-  a.meta = tb + L.off_meta;
-  a.meta_slot = L.meta_slot;
-  a.streams = reinterpret_cast<uint16_t*>(tb + L.off_streams);
-  a.unit_words = L.unit_words;
-  a.sub_words = L.sub_words;
-  a.lane_words = L.lane_words;
-  a.comp_bytes = reinterpret_cast<int32_t*>(tb + L.off_comp);
-  a.part_hist = reinterpret_cast<uint32_t*>(tb + L.off_hist);
-  if (int rc = launch_encode<1, false>(a, count, s)) return rc;
-  PackArgs p{};
-  p.C = chunk_bytes;
-  p.nch = count;
-  p.comp_bytes = a.comp_bytes;
-  p.meta = a.meta;
-  p.meta_slot = a.meta_slot;
-  p.streams = a.streams;
-  p.unit_words = a.unit_words;
-  p.sub_words = a.sub_words;
-  p.lane_words = a.lane_words;
-  p.t = t;
-  assemble_kernel<<<unsigned(count), kPackThreads, 0, s>>>(p, in_bytes, out_ptrs, out_bytes, statuses);
+  bind_scratch(a, tb + job_table_bytes(1), count);
+  EncArgs* dj = reinterpret_cast<EncArgs*>(tb);
+  if (int rc = upload_jobs(&a, 1, dj, s)) return rc;
+  if (int rc = launch_encode<1, false>(dj, 1, count, s)) return rc;
+  assemble_kernel<<<unsigned(count), kPackThreads, 0, s>>>(dj, in_bytes, out_ptrs, out_bytes, statuses);
   count_launch();
   return check_launch("zn_ans_compress");
 }
@@ -987,103 +989,99 @@ int64_t zn_compress_bound(int64_t n, int k, int ndim, int64_t chunk_bytes) {
   return head + data;
 }
 
-size_t zn_compress_temp_bytes(int64_t n, int k, int64_t chunk_bytes, int sub_chunks) {
+size_t zn_compress_batch_temp_bytes(int njobs, const int64_t* n, int k, int64_t chunk_bytes, int sub_chunks) {
   const int t = sub_log2(sub_chunks);
-  if (t < 0 || n < 0 || k <= 0 || chunk_bytes <= 0) return 0;
-  return enc_layout(int64_t(k) * cdiv(n, chunk_bytes), chunk_bytes, t).total;
+  if (t < 0 || njobs < 0 || k <= 0 || chunk_bytes <= 0) return 0;
+  size_t total = job_table_bytes(njobs);
+  for (int i = 0; i < njobs; ++i) {
+    if (n[i] < 0) return 0;
+    total += enc_layout(int64_t(k) * cdiv(n[i], chunk_bytes), chunk_bytes, t).total;
+  }
+  return total;
+}
+
+size_t zn_compress_temp_bytes(int64_t n, int k, int64_t chunk_bytes, int sub_chunks) {
+  return zn_compress_batch_temp_bytes(1, &n, k, chunk_bytes, sub_chunks);
+}
+
+int zn_compress_batch(int njobs, const void* const* x, const int64_t* n, int k, int reorder, const void* const* headers,
+                      const int* header_bytes, int64_t chunk_bytes, int sub_chunks, double threshold, void* const* out,
+                      const int64_t* out_capacity, uint64_t* sizes_out, void* temp, size_t temp_bytes, void* stream) {
+  const int t = sub_log2(sub_chunks);
+  if (njobs < 0 || t < 0 || !valid_k(k, reorder) || chunk_bytes <= 0 || chunk_bytes > kMaxChunkBytes ||
+      chunk_bytes % 8 || !(threshold > 0.0 && threshold <= 1.0))
+    return set_error(ZN_ERR_INVALID, "zn_compress: bad arguments");
+  if (njobs == 0) return ZN_OK;
+  if (!temp || temp_bytes < zn_compress_batch_temp_bytes(njobs, n, k, chunk_bytes, sub_chunks))
+    return set_error(ZN_ERR_SPACE, "zn_compress: temp buffer too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* tb = static_cast<uint8_t*>(temp);
+  uint8_t* region = tb + job_table_bytes(njobs);
+  std::vector<EncArgs> jobs(static_cast<size_t>(njobs));
+  int64_t chunk0 = 0;
+  for (int i = 0; i < njobs; ++i) {
+    const int hb = header_bytes[i];
+    if (n[i] < 0 || hb < 24 || hb > 24 + 8 * 64 || (hb - 24) % 8 || (reinterpret_cast<uintptr_t>(x[i]) & 7) ||
+        (reinterpret_cast<uintptr_t>(out[i]) & 7))
+      return set_error(ZN_ERR_INVALID, "zn_compress: bad arguments (job %d)", i);
+    if (out_capacity[i] < zn_compress_bound(n[i], k, (hb - 24) / 8, chunk_bytes))
+      return set_error(ZN_ERR_SPACE, "zn_compress: output buffer too small (job %d)", i);
+    EncArgs& a = jobs[size_t(i)];
+    memset(&a, 0, sizeof(a));
+    a.x = static_cast<const uint8_t*>(x[i]);
+    a.n = n[i];
+    a.C = chunk_bytes;
+    a.nch = cdiv(n[i], chunk_bytes);
+    a.units = int64_t(k) * a.nch;
+    a.chunk0 = chunk0;
+    a.t = t;
+    a.allow_skip = 1;
+    a.threshold = threshold;
+    bind_scratch(a, region, a.units);
+    region += enc_layout(a.units, chunk_bytes, t).total;
+    a.out = static_cast<uint8_t*>(out[i]);
+    a.size_out = sizes_out + i;
+    a.sizes_off = hb;
+    a.idx_off = hb + 4 * a.units;
+    a.header_len = hb;
+    memcpy(a.header, headers[i], size_t(hb));
+    chunk0 += a.nch;
+  }
+  if (chunk0 > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_compress: too many chunks");
+  EncArgs* dj = reinterpret_cast<EncArgs*>(tb);
+  if (int rc = upload_jobs(jobs.data(), njobs, dj, s)) return rc;
+  int rc = ZN_OK;
+  switch (k * 2 + (reorder ? 1 : 0)) {
+    case 2: rc = launch_encode<1, false>(dj, njobs, chunk0, s); break;
+    case 4: rc = launch_encode<2, false>(dj, njobs, chunk0, s); break;
+    case 5: rc = launch_encode<2, true>(dj, njobs, chunk0, s); break;
+    case 8: rc = launch_encode<4, false>(dj, njobs, chunk0, s); break;
+    case 9: rc = launch_encode<4, true>(dj, njobs, chunk0, s); break;
+    default: rc = launch_encode<8, false>(dj, njobs, chunk0, s); break;
+  }
+  if (rc) return rc;
+  {
+    TimedLaunch tl("scan", s);
+    scan_kernel<<<unsigned(njobs), kScanThreads, 0, s>>>(dj);
+  }
+  count_launch();
+  if ((rc = check_launch("scan_kernel"))) return rc;
+  switch (k * 2 + (reorder ? 1 : 0)) {
+    case 2: launch_pack<1, false>(dj, njobs, chunk0, s); break;
+    case 4: launch_pack<2, false>(dj, njobs, chunk0, s); break;
+    case 5: launch_pack<2, true>(dj, njobs, chunk0, s); break;
+    case 8: launch_pack<4, false>(dj, njobs, chunk0, s); break;
+    case 9: launch_pack<4, true>(dj, njobs, chunk0, s); break;
+    default: launch_pack<8, false>(dj, njobs, chunk0, s); break;
+  }
+  return check_launch("pack_kernel");
 }
 
 int zn_compress(const void* x, int64_t n, int k, int reorder, const void* header, int header_bytes,
                 int64_t chunk_bytes, int sub_chunks, double threshold, void* out, int64_t out_capacity,
                 uint64_t* size_out, void* temp, size_t temp_bytes, void* stream) {
-  const int t = sub_log2(sub_chunks);
-  if (t < 0 || n < 0 || (k != 1 && k != 2 && k != 4 && k != 8) || (reorder && k != 2 && k != 4) ||
-      chunk_bytes <= 0 || chunk_bytes > kMaxChunkBytes || chunk_bytes % 8 || !(threshold > 0.0 && threshold <= 1.0) ||
-      header_bytes < 24 || header_bytes > 24 + 8 * 64 || (header_bytes - 24) % 8 ||
-      (reinterpret_cast<uintptr_t>(x) & 7) || (reinterpret_cast<uintptr_t>(out) & 7))
-    return set_error(ZN_ERR_INVALID, "zn_compress: bad arguments");
-  const int ndim = (header_bytes - 24) / 8;
-  if (out_capacity < zn_compress_bound(n, k, ndim, chunk_bytes))
-    return set_error(ZN_ERR_SPACE, "zn_compress: output buffer too small");
-  const int64_t nch = cdiv(n, chunk_bytes), total = int64_t(k) * nch;
-  if (nch > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_compress: too many chunks");
-  const EncLayout L = enc_layout(total, chunk_bytes, t);
-  if (!temp || temp_bytes < L.total) return set_error(ZN_ERR_SPACE, "zn_compress: temp buffer too small");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* tb = static_cast<uint8_t*>(temp);
-
-  EncArgs a{};
-  a.x = static_cast<const uint8_t*>(x);
-  a.n = n;
-  a.C = chunk_bytes;
-  a.nch = nch;
-  a.t = t;
-  a.threshold = threshold;
-  a.allow_skip = true;
-  a.meta = tb + L.off_meta;
-  a.meta_slot = L.meta_slot;
-  a.streams = reinterpret_cast<uint16_t*>(tb + L.off_streams);
-  a.unit_words = L.unit_words;
-  a.sub_words = L.sub_words;
-  a.lane_words = L.lane_words;
-  a.comp_bytes = reinterpret_cast<int32_t*>(tb + L.off_comp);
-  a.part_hist = reinterpret_cast<uint32_t*>(tb + L.off_hist);
-  int rc = ZN_OK;
-  if (nch > 0) {
-    switch (k * 2 + (reorder ? 1 : 0)) {
-      case 2: rc = launch_encode<1, false>(a, nch, s); break;
-      case 4: rc = launch_encode<2, false>(a, nch, s); break;
-      case 5: rc = launch_encode<2, true>(a, nch, s); break;
-      case 8: rc = launch_encode<4, false>(a, nch, s); break;
-      case 9: rc = launch_encode<4, true>(a, nch, s); break;
-      default: rc = launch_encode<8, false>(a, nch, s); break;
-    }
-    if (rc) return rc;
-  }
-  ScanArgs sa{};
-  sa.comp_bytes = a.comp_bytes;
-  sa.total = total;
-  sa.nch = nch;
-  sa.C = chunk_bytes;
-  sa.n = n;
-  sa.threshold = threshold;
-  sa.sizes_off = header_bytes;
-  sa.idx_off = header_bytes + 4 * total;
-  sa.out = static_cast<uint8_t*>(out);
-  sa.dst_rel = reinterpret_cast<int64_t*>(tb + L.off_dst);
-  sa.scalars = reinterpret_cast<int64_t*>(tb + L.off_scalars);
-  sa.size_out = size_out;
-  memcpy(sa.header.bytes, header, size_t(header_bytes));
-  sa.header.len = header_bytes;
-  scan_kernel<<<1, kScanThreads, 0, s>>>(sa);
-  count_launch();
-  if ((rc = check_launch("scan_kernel"))) return rc;
-  if (nch == 0) return ZN_OK;
-  PackArgs p{};
-  p.x = a.x;
-  p.n = n;
-  p.C = chunk_bytes;
-  p.nch = nch;
-  p.comp_bytes = a.comp_bytes;
-  p.dst_rel = sa.dst_rel;
-  p.scalars = sa.scalars;
-  p.meta = a.meta;
-  p.meta_slot = a.meta_slot;
-  p.streams = a.streams;
-  p.unit_words = a.unit_words;
-  p.sub_words = a.sub_words;
-  p.lane_words = a.lane_words;
-  p.t = t;
-  p.out = sa.out;
-  switch (k * 2 + (reorder ? 1 : 0)) {
-    case 2: launch_pack<1, false>(p, nch, s); break;
-    case 4: launch_pack<2, false>(p, nch, s); break;
-    case 5: launch_pack<2, true>(p, nch, s); break;
-    case 8: launch_pack<4, false>(p, nch, s); break;
-    case 9: launch_pack<4, true>(p, nch, s); break;
-    default: launch_pack<8, false>(p, nch, s); break;
-  }
-  return check_launch("pack_kernel");
+  return zn_compress_batch(1, &x, &n, k, reorder, &header, &header_bytes, chunk_bytes, sub_chunks, threshold, &out,
+                           &out_capacity, size_out, temp, temp_bytes, stream);
 }
 
 }  // extern "C"

@@ -41,6 +41,13 @@ int zn_version(void);
 const char *zn_last_error(void);
 /* Number of kernels this library has launched in this process (all devices). */
 uint64_t zn_launch_count(void);
+/* Kernel timing for measurement (no reference counterpart): while enabled, every launch of the
+ * named kernel kind ("hist", "encode", "scan", "pack", "dscan", "decode", "decode_overflow",
+ * "crc", or "*" for all) is bracketed by CUDA events on its launching stream.  zn_timing_read
+ * waits for the recorded events of one kind (NULL: all) and returns their summed duration and
+ * count, then forgets them. */
+int zn_timing_enable(const char *kernel, int enable);
+int zn_timing_read(const char *kernel, double *total_ms, int64_t *launches);
 
 /* ---- byte-plane seam: replaces src/cuzipnn/_kernels.py:134-188 -------------------------- */
 
@@ -101,6 +108,16 @@ int zn_compress(const void *x, int64_t n, int k, int reorder, const void *header
                 int64_t chunk_bytes, int sub_chunks, double passthrough_threshold, void *out,
                 int64_t out_capacity, uint64_t *size_out, void *temp, size_t temp_bytes, void *stream);
 
+/* Batched form of zn_compress: njobs tensors of the same element size and settings, compressed
+ * by one launch per stage (the reference compresses one tensor per call, src/cuzipnn/_codec.py:
+ * 231-413).  x, n, headers, header_bytes, out and out_capacity are host arrays with one entry per
+ * tensor; sizes_out is a device array of njobs u64. */
+size_t zn_compress_batch_temp_bytes(int njobs, const int64_t *n, int k, int64_t chunk_bytes, int sub_chunks);
+int zn_compress_batch(int njobs, const void *const *x, const int64_t *n, int k, int reorder,
+                      const void *const *headers, const int *header_bytes, int64_t chunk_bytes, int sub_chunks,
+                      double passthrough_threshold, void *const *out, const int64_t *out_capacity,
+                      uint64_t *sizes_out, void *temp, size_t temp_bytes, void *stream);
+
 size_t zn_decompress_temp_bytes(int64_t n, int k, int64_t chunk_bytes);
 /* Decompress the non-stored blob at blob (device, 8-byte aligned, blob_bytes long) whose header
  * fields are given, into out (n * k bytes, device).  Decoding errors are OR-ed into the device
@@ -108,6 +125,13 @@ size_t zn_decompress_temp_bytes(int64_t n, int k, int64_t chunk_bytes);
 int zn_decompress(const void *blob, int64_t blob_bytes, int64_t n, int k, int reorder, int ndim,
                   int64_t chunk_bytes, int64_t n_comp, void *out, int32_t *status, void *temp,
                   size_t temp_bytes, void *stream);
+
+/* Batched form of zn_decompress: njobs non-stored blobs of one element size (host arrays, one
+ * entry per blob; status is a device array of njobs int32 that the caller zeroes). */
+size_t zn_decompress_batch_temp_bytes(int njobs, const int64_t *n, int k, const int64_t *chunk_bytes);
+int zn_decompress_batch(int njobs, const void *const *blobs, const int64_t *blob_bytes, const int64_t *n, int k,
+                        int reorder, const int *ndim, const int64_t *chunk_bytes, const int64_t *n_comp,
+                        void *const *out, int32_t *status, void *temp, size_t temp_bytes, void *stream);
 
 #ifdef __cplusplus
 }

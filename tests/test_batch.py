@@ -1,0 +1,72 @@
+"""Batched API (compress_tensors / decompress_tensors): every blob equals the per-tensor one, and
+round trips are exact, across element sizes, stored and empty tensors and mixed devices."""
+
+import pytest
+import torch
+
+import cuzipnn_b200 as z
+
+pytestmark = pytest.mark.gpu
+
+INT_OF = {1: torch.uint8, 2: torch.int16, 4: torch.int32, 8: torch.int64}
+
+
+def bits(t):
+    return t.contiguous().view(INT_OF[t.element_size()])
+
+
+def mixed_tensors():
+    g = torch.Generator(device="cuda").manual_seed(7)
+    def w(*shape, dtype=torch.bfloat16, scale=0.02):
+        return (torch.randn(*shape, device="cuda", generator=g) * scale).to(dtype)
+    return [
+        w(1000, 777),
+        w(3584),                                  # stored (below min_compress_bytes)
+        w(300, 301, dtype=torch.float32),
+        torch.empty(0, 5, device="cuda", dtype=torch.bfloat16),
+        w(257, 1024, dtype=torch.float16),
+        (torch.randn(400, 513, device="cuda", generator=g) * 16).clamp(-448, 448).to(torch.float8_e4m3fn),
+        w(1, 131072 * 3 + 5),
+        torch.randint(-100, 100, (70_001,), device="cuda", generator=g).to(torch.int32),
+        w(64, 64).t(),                            # non-contiguous
+        w(5, 131072 + 64).cpu(),                  # CPU input
+    ]
+
+
+@pytest.mark.parametrize("readback", [True, False])
+def test_batch_blobs_equal_single(readback):
+    ts = mixed_tensors()
+    batch = z.compress_tensors(ts, readback_to_cpu=readback)
+    for t, b in zip(ts, batch):
+        single = z.compress_tensor(t, readback_to_cpu=readback)
+        assert b.is_cuda == (not readback) or b.numel() == single.numel()
+        assert torch.equal(b.cpu(), single.cpu())
+    ys = z.decompress_tensors(batch)
+    assert z.last_decode_status() == 0
+    for t, y in zip(ts, ys):
+        assert y.dtype == t.dtype and y.shape == t.shape and y.is_cuda
+        assert torch.equal(bits(y).cpu(), bits(t).cpu())
+
+
+def test_batch_small_chunks_and_options():
+    ts = mixed_tensors()
+    kw = dict(chunk_bytes=4096, sub_chunk_bytes=1000, passthrough_threshold=0.5, min_compress_bytes=0)
+    batch = z.compress_tensors(ts, **kw)
+    for t, b in zip(ts, batch):
+        assert torch.equal(b, z.compress_tensor(t, **kw))
+    ys = z.decompress_tensors([b.cuda() for b in batch], readback_to_cpu=True)
+    for t, y in zip(ts, ys):
+        assert y.device.type == "cpu" and torch.equal(bits(y), bits(t).cpu())
+
+
+def test_batch_many_tensors():
+    g = torch.Generator(device="cuda").manual_seed(3)
+    ts = [(torch.randn(int(s), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+          for s in torch.randint(40_000, 600_000, (150,), generator=torch.Generator().manual_seed(1))]
+    batch = z.compress_tensors(ts, readback_to_cpu=False)
+    ys = z.decompress_tensors(batch)
+    torch.cuda.synchronize()
+    assert z.last_decode_status() == 0
+    for t, y in zip(ts, ys):
+        assert torch.equal(bits(y), bits(t))
+    assert torch.equal(batch[17].cpu(), z.compress_tensor(ts[17]))
