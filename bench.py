@@ -41,11 +41,13 @@ WORKLOAD = (
 )
 
 
-def model_shapes() -> list[tuple[str, tuple[int, ...], str]]:
-    """(name, shape, init) of the 7B bf16 decoder, in checkpoint order."""
+def model_shapes(layers: int | None = None) -> list[tuple[str, tuple[int, ...], str]]:
+    """(name, shape, init) of the 7B bf16 decoder, in checkpoint order.  With `layers`, only that
+    many decoder layers and no embedding / LM head (smaller cases for profiler captures)."""
     kv = KV_HEADS * HEAD_DIM
-    out = [("model.embed_tokens.weight", (VOCAB, HIDDEN), "normal")]
-    for i in range(LAYERS):
+    full = layers is None
+    out = [("model.embed_tokens.weight", (VOCAB, HIDDEN), "normal")] if full else []
+    for i in range(LAYERS if full else layers):
         p = f"model.layers.{i}."
         out += [
             (p + "self_attn.q_proj.weight", (HIDDEN, HIDDEN), "normal"),
@@ -61,7 +63,8 @@ def model_shapes() -> list[tuple[str, tuple[int, ...], str]]:
             (p + "input_layernorm.weight", (HIDDEN,), "ones"),
             (p + "post_attention_layernorm.weight", (HIDDEN,), "ones"),
         ]
-    out += [("model.norm.weight", (HIDDEN,), "ones"), ("lm_head.weight", (VOCAB, HIDDEN), "normal")]
+    if full:
+        out += [("model.norm.weight", (HIDDEN,), "ones"), ("lm_head.weight", (VOCAB, HIDDEN), "normal")]
     return out
 
 
@@ -72,8 +75,8 @@ def make_tensor(idx: int, shape, init: str, device) -> torch.Tensor:
     return (torch.randn(shape, generator=g, device=device) * 0.02).to(torch.bfloat16)
 
 
-def build_model(device) -> list[torch.Tensor]:
-    return [make_tensor(i, s, init, device) for i, (_, s, init) in enumerate(model_shapes())]
+def build_model(device, layers: int | None = None) -> list[torch.Tensor]:
+    return [make_tensor(i, s, init, device) for i, (_, s, init) in enumerate(model_shapes(layers))]
 
 
 def nbytes(ts) -> int:
@@ -101,7 +104,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"],
+                 "-lms", "50"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -147,13 +150,17 @@ def measured_hbm_peak() -> tuple[float, str]:
         return 6650.0, "fallback 6.65 TB/s"
 
 
-def profile_traffic(kernel: str) -> dict | None:
-    """DRAM traffic per algorithmic byte of a kernel from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", f"{kernel}_traffic.json")
-    try:
-        return json.load(open(path))
-    except (OSError, ValueError):
-        return None
+def profile_traffic(kernel: str) -> float | None:
+    """DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic byte of a kernel,
+    from the `traffic_per_algo_byte:` line of its committed ncu summary profiles/<kernel>_*.md."""
+    import glob
+    import re
+
+    for path in sorted(glob.glob(os.path.join(ROOT, "profiles", f"{kernel}_*.md"))):
+        m = re.search(r"^traffic_per_algo_byte:\s*([0-9.]+)", open(path).read(), re.M)
+        if m:
+            return float(m.group(1))
+    return None
 
 
 def cpu_round_trip(tensors, threads: int) -> tuple[float, float, int, int]:
@@ -226,11 +233,15 @@ METRIC = "compress / decompress GB/s (original bytes) per B200 and 8-GPU box; ra
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-one-at-a-time", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="profile a smaller model: this many decoder layers, no embedding / LM head")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     if args.impl == "reference":
@@ -265,7 +276,7 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    model = build_model(device)
+    model = build_model(device, args.layers)
     model_bytes = nbytes(model)
     torch.cuda.synchronize()
 
@@ -278,7 +289,7 @@ def main() -> None:
 
     # Correctness once, outside the timed region.
     blobs, outs, _ = step()
-    for i in (0, 1, 8, 338):
+    for i in sorted({0, 1, 8, len(model) - 1}):
         assert torch.equal(outs[i].view(torch.int16), model[i].view(torch.int16)), i
     assert z.last_decode_status(device) == 0
     blob_bytes = sum(b.numel() for b in blobs)
@@ -322,7 +333,7 @@ def main() -> None:
     peak, peak_src = measured_hbm_peak()
     achieved = algo / per_launch_s / GB
     tr = profile_traffic(dominant + "_kernel")
-    traffic = round(tr["traffic_per_algo_byte"] * algo) if tr else None
+    traffic = round(tr * algo) if tr else None
     roofline = {"bound": "hbm", "kernel": dominant + "_kernel", "achieved": round(achieved, 1),
                 "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "traffic": traffic, "algo_bytes_per_launch": algo,
@@ -331,7 +342,7 @@ def main() -> None:
 
     # One tensor at a time (the reference's own methodology), device time.
     ev1 = []
-    for _ in range(1):
+    for _ in range(0 if args.no_one_at_a_time else 1):
         a = torch.cuda.Event(enable_timing=True)
         m = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
@@ -344,17 +355,17 @@ def main() -> None:
         torch.cuda.synchronize()
         ev1.append((a.elapsed_time(m) / 1e3, m.elapsed_time(b) / 1e3))
         del bl
-    one_c = max_over_ranks(min(v[0] for v in ev1))
-    one_d = max_over_ranks(min(v[1] for v in ev1))
+    one_c = max_over_ranks(min(v[0] for v in ev1)) if ev1 else None
+    one_d = max_over_ranks(min(v[1] for v in ev1)) if ev1 else None
 
     # End to end through the public API from pinned host memory: H2D of the inputs, CPU blobs,
     # H2D of the blobs, and a D2H read of a result word each step.
-    host = [t.cpu().pin_memory() for t in model]
+    host = [t.cpu().pin_memory() for t in model] if not args.no_e2e else []
     torch.cuda.synchronize()
     barrier()
     e2e_times = []
     h2d = d2h = 0
-    for s_i in range(args.e2e_steps + 1):
+    for s_i in range(0 if args.no_e2e else args.e2e_steps + 1):
         t0 = time.perf_counter()
         cblobs = z.compress_tensors(host, readback_to_cpu=True, pin_memory=True)
         outs = z.decompress_tensors(cblobs)
@@ -367,10 +378,12 @@ def main() -> None:
         h2d, d2h = model_bytes + sz, sz + check.numel()
         del cblobs, outs
     del host
-    t_e2e = max_over_ranks(sum(e2e_times) / len(e2e_times))
-    e2e = {"value": round(world * model_bytes / t_e2e / GB, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-           "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e * 1e3, 1),
-           "path": "pinned host tensors -> compress_tensors(readback_to_cpu, pin_memory) -> decompress_tensors"}
+    e2e = None
+    if e2e_times:
+        t_e2e = max_over_ranks(sum(e2e_times) / len(e2e_times))
+        e2e = {"value": round(world * model_bytes / t_e2e / GB, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e * 1e3, 1),
+               "path": "pinned host tensors -> compress_tensors(readback_to_cpu, pin_memory) -> decompress_tensors"}
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -394,13 +407,18 @@ def main() -> None:
             "vs_baseline": None,
             "dtype": "u8",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "value": "original bytes / (compress + decompress time)",
-                       "l2": "inputs 15.2 GB per GPU >> 126 MB L2 (no flush)", "parallelism": f"{world} x replica"},
+            "config": {"workload": WORKLOAD if args.layers is None else
+                       f"first {args.layers} decoder layer(s) only ({len(model)} tensors, {model_bytes / GB:.3f} GB) of: "
+                       + WORKLOAD,
+                       "value": "original bytes / (compress + decompress time)",
+                       "l2": f"inputs {model_bytes / GB:.3g} GB per GPU >> 126 MB L2 (no flush)",
+                       "parallelism": f"{world} x replica"},
             "compress_gbs": round(world * model_bytes / t_comp / GB, 3),
             "decompress_gbs": round(world * model_bytes / t_dec / GB, 3),
             "ratio": round(ratio, 5),
-            "one_tensor_at_a_time": {"compress_gbs": round(world * model_bytes / one_c / GB, 3),
-                                     "decompress_gbs": round(world * model_bytes / one_d / GB, 3)},
+            "one_tensor_at_a_time": None if one_c is None else {
+                "compress_gbs": round(world * model_bytes / one_c / GB, 3),
+                "decompress_gbs": round(world * model_bytes / one_d / GB, 3)},
             "roofline": roofline,
             "cpu_baseline": cpu_baseline,
             "clocks": clocks.summary(),
