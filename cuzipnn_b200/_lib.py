@@ -40,6 +40,7 @@ SIGNATURES = {
     "zn_ans_decompress": (_i32, [_p, _p, _p, _i64, _p, _p, _p, _sz, _p]),
     "zn_crc32_temp_bytes": (_sz, [_i64, _i64]),
     "zn_crc32": (_i32, [_p, _i64, _i64, _p, _p, _sz, _p]),
+    "zn_crc32_noalloc": (_i32, [_p, _i64, _i64, _p, _p]),
     "zn_compress_bound": (_i64, [_i64, _i32, _i32, _i64]),
     "zn_compress_temp_bytes": (_sz, [_i64, _i32, _i64, _i32]),
     "zn_compress": (_i32, [_p, _i64, _i32, _i32, _p, _i32, _i64, _i32, ctypes.c_double, _p, _i64, _p, _p, _sz, _p]),

@@ -244,3 +244,86 @@ int zn_crc32(const void* data, int64_t nbytes, int64_t segment_bytes, uint32_t* 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// zn_crc32_noalloc: the same two kernels with their partial-CRC scratch in a static device array,
+// for callers that must not allocate device memory (see the declaration in the public header).
+//
+// The array is 2 MiB: 524,288 u32 slots, one per 32 KiB block of every segment longer than
+// 32 KiB.  Each GPU that runs this code holds it until the process exits.  All calls on a device
+// share it and it keeps the previous call's contents; every slot a call reads is written earlier
+// in the same call (level 1 writes all nseg * blocks_per_seg slots before level 2 reads them, in
+// stream order), so nothing needs clearing.  Two calls whose kernels overlap on the GPU (different
+// streams, or host threads with no ordering between them) race on the array.
+
+#include <mutex>
+
+namespace {
+
+constexpr int64_t kNoAllocSlots = int64_t(1) << 19;  // 2 MiB of u32
+constexpr int kNoAllocMaxDevices = 64;
+
+}  // namespace
+
+static __device__ __align__(256) uint32_t g_crc_noalloc_scratch[kNoAllocSlots];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+uint32_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device, resolved on the first call per
+// device (this loads the module on that device if it is not loaded yet).
+int noalloc_scratch(uint32_t** ptr) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(ZN_ERR_CUDA, "zn_crc32_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(ZN_ERR_INVALID, "zn_crc32_noalloc: device %d is beyond the %d this entry point supports", dev,
+                     kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_crc_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(ZN_ERR_CUDA, "zn_crc32_noalloc: cudaGetSymbolAddress of the scratch array on device %d: %s",
+                       dev, cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<uint32_t*>(p);
+  }
+  *ptr = g_noalloc_ptr[dev];
+  return ZN_OK;
+}
+
+}  // namespace
+
+extern "C" int zn_crc32_noalloc(const void* data, int64_t nbytes, int64_t segment_bytes, uint32_t* out,
+                                void* stream) {
+  if (nbytes < 0 || segment_bytes <= 0) return set_error(ZN_ERR_INVALID, "zn_crc32_noalloc: bad arguments");
+  if (nbytes == 0) return ZN_OK;
+  const int64_t nseg = cdiv(nbytes, segment_bytes);
+  const int64_t seg = min(segment_bytes, nbytes);  // longest segment
+  const int64_t bps = seg > kBlock ? cdiv(seg, kBlock) : 0;
+  if (nseg * bps > kNoAllocSlots)
+    return set_error(ZN_ERR_INVALID,
+                     "zn_crc32_noalloc: %lld bytes in segments of %lld need %lld scratch slots (one per 32 KiB block "
+                     "of each segment); the static scratch holds %lld (2 MiB). Use zn_crc32 with a temp buffer",
+                     (long long)nbytes, (long long)segment_bytes, (long long)(nseg * bps), (long long)kNoAllocSlots);
+  uint32_t* partial = nullptr;
+  if (int rc = noalloc_scratch(&partial)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint8_t* d = static_cast<const uint8_t*>(data);
+  if (bps == 0) {  // every segment fits one CTA: the scratch is not touched
+    int G = 1;
+    while (int64_t(G) * kPiece < seg) G <<= 1;
+    const int64_t grid = cdiv(nseg, int64_t(kThreads / G));
+    if (grid > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_crc32_noalloc: too many segments");
+    crc_level1<<<unsigned(grid), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, G, 1, true, out, nullptr);
+    count_launch();
+    return check_launch("zn_crc32_noalloc");
+  }
+  crc_level1<<<unsigned(nseg * bps), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, kThreads, bps, false, out,
+                                                        partial);
+  crc_level2<<<unsigned(nseg), kThreads, 0, st>>>(nbytes, segment_bytes, nseg, bps, partial, out);
+  count_launch(2);
+  return check_launch("zn_crc32_noalloc");
+}

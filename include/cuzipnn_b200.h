@@ -94,6 +94,21 @@ size_t zn_crc32_temp_bytes(int64_t nbytes, int64_t segment_bytes);
  * [i * segment_bytes, min((i + 1) * segment_bytes, nbytes)) of data; any alignment. */
 int zn_crc32(const void *data, int64_t nbytes, int64_t segment_bytes, uint32_t *out, void *temp,
              size_t temp_bytes, void *stream);
+/* zn_crc32 without the temp buffer.  No counterpart in the reference (there nvCOMP always takes
+ * its temp space from torch's allocator).  It is for callers that cannot allocate device memory:
+ * a checksum step inside a process whose GPU memory is already owned by another allocator (a
+ * serving engine that reserves the free memory up front for weights and KV cache, so that a
+ * cudaMalloc fails, and a cudaFree would stall every stream of the device), and C hosts bound
+ * through ctypes, cgo or JNI that hold only the device pointers they were handed.  It allocates
+ * nothing: its scratch is one fixed 2 MiB array of device memory (524,288 slots, one per 32 KiB
+ * block of each segment longer than 32 KiB, e.g. up to 16 GiB of data in segments that are a
+ * multiple of 32 KiB), which every GPU that runs it holds until the process exits.  A call that
+ * needs more slots returns ZN_ERR_INVALID and launches nothing.  The first call on each device
+ * looks up the array's address there (loading the library's device code if needed), so make that
+ * first call before any stream capture.  All calls on a device share the array: calls whose
+ * kernels overlap on the GPU (other streams, or host threads with no ordering between them) race
+ * and return wrong CRCs.  Segments of at most 32 KiB do not touch the array. */
+int zn_crc32_noalloc(const void *data, int64_t nbytes, int64_t segment_bytes, uint32_t *out, void *stream);
 
 /* ---- whole-tensor codec: replaces src/cuzipnn/_codec.py:308-413 and :471-530 ------------- */
 
