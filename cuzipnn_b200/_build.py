@@ -6,9 +6,11 @@ without a GPU.  The package loads it with ctypes; there is no JIT cache and no f
 
 from __future__ import annotations
 
+import concurrent.futures
 import os
 import subprocess
 import sys
+import tempfile
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
@@ -37,13 +39,26 @@ def _stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
-    """Compile the library if any source is newer than it; returns its path."""
+    """Compile the library if any source is newer than it; returns its path.  The translation
+    units compile in parallel into a temporary folder, then link into the package folder."""
     if not force and not _stale():
         return LIB
-    cmd = [_nvcc(), *ARCH, *FLAGS, "-o", LIB + ".tmp", *[os.path.join(CSRC, f) for f in SOURCES]]
-    if verbose:
-        print(" ".join(cmd), file=sys.stderr)
-    subprocess.run(cmd, check=True)
+    nvcc = _nvcc()
+    compile_flags = [f for f in FLAGS if f != "-shared"]
+    with tempfile.TemporaryDirectory() as tmp:
+        cmds = [[nvcc, *ARCH, *compile_flags, "-c", os.path.join(CSRC, f), "-o", os.path.join(tmp, f + ".o")]
+                for f in SOURCES]
+        if verbose:
+            for c in cmds:
+                print(" ".join(c), file=sys.stderr)
+        with concurrent.futures.ThreadPoolExecutor(len(cmds)) as ex:
+            for r in ex.map(lambda c: subprocess.run(c), cmds):
+                if r.returncode:
+                    raise subprocess.CalledProcessError(r.returncode, r.args)
+        link = [nvcc, *ARCH, "-shared", "-o", LIB + ".tmp", *[os.path.join(tmp, f + ".o") for f in SOURCES]]
+        if verbose:
+            print(" ".join(link), file=sys.stderr)
+        subprocess.run(link, check=True)
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

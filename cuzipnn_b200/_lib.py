@@ -56,7 +56,7 @@ SIGNATURES = {
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m cuzipnn_b200._build` "
+            f"{LIB_PATH} is missing: build it with `python cuzipnn_b200/_build.py` "
             "(or __graft_entry__.build()); the codec has no fallback"
         )
     lib = ctypes.CDLL(LIB_PATH)
