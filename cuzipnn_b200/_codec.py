@@ -472,6 +472,55 @@ def _ptr_array(ctype, values):
     return (ctype * len(values))(*values)
 
 
+_COPY_BATCH_MAX = 1 << 29  # largest single copy of one zn_copy_chunks launch (65535 tiles of 8 KiB)
+
+
+def _copy_batch(device: torch.device, srcs: list[int], dsts: list[int], sizes: list[int]) -> None:
+    """Many small device copies (8-byte aligned addresses) in one zn_copy_chunks launch; the address
+    table goes to the GPU in one pinned copy."""
+    n = len(srcs)
+    if n == 0:
+        return
+    host = torch.tensor(srcs + dsts + sizes, dtype=torch.int64).pin_memory()
+    tbl = host.to(device, non_blocking=True)
+    base = tbl.data_ptr()
+    _lib.check(
+        _lib.lib.zn_copy_chunks(base, base + 8 * n, base + 16 * n, n, max(sizes), 0, _stream(device)),
+        "zn_copy_chunks",
+    )
+
+
+def _stored_blobs_gpu(items: list[tuple[int, torch.Tensor, bytes]], device: torch.device) -> dict[int, torch.Tensor]:
+    """Blobs of the stored path (header + raw bytes) for many tensors, built on the GPU by one
+    header upload and one batched copy.  Each blob is a view into one shared buffer."""
+    offs, pos = [], 0
+    for _, x, head in items:
+        offs.append(pos)
+        pos += (len(head) + x.numel() * x.element_size() + 255) & ~255
+    out = torch.empty(max(pos, 1), dtype=torch.uint8, device=device)
+    heads = b"".join(h for _, _, h in items)
+    hdev = torch.frombuffer(bytearray(heads), dtype=torch.uint8).pin_memory().to(device, non_blocking=True)
+    srcs, dsts, sizes = [], [], []
+    hpos = 0
+    for (_, x, head), o in zip(items, offs):
+        srcs.append(hdev.data_ptr() + hpos)
+        dsts.append(out.data_ptr() + o)
+        sizes.append(len(head))
+        hpos += len(head)
+        nb = x.numel() * x.element_size()
+        if nb:
+            x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+            if x.data_ptr() % 8:
+                x = x.clone()
+            srcs.append(x.data_ptr())
+            dsts.append(out.data_ptr() + o + len(head))
+            sizes.append(nb)
+    # `hdev` and the staged inputs were allocated on this stream, so the caching allocator reuses
+    # their memory only after the copy has run.
+    _copy_batch(device, srcs, dsts, sizes)
+    return {i: out[o : o + len(head) + x.numel() * x.element_size()] for (i, x, head), o in zip(items, offs)}
+
+
 def compress_tensors(
     tensors: list[torch.Tensor],
     *,
@@ -489,19 +538,43 @@ def compress_tensors(
     With readback_to_cpu=False the blobs are views into one shared GPU buffer."""
     blobs: list[torch.Tensor | None] = [None] * len(tensors)
     groups: dict[tuple[int, bool], list[int]] = {}
+    small: list[int] = []  # stored path and empty tensors, handled after the coded launches
     sub_chunks = _sub_chunks(chunk_bytes, sub_chunk_bytes) if sub_chunk_bytes > 0 else 0
     for i, t in enumerate(tensors):
         dev, sub_chunks = _check_args(t, chunk_bytes, sub_chunk_bytes, passthrough_threshold, min_compress_bytes,
                                       None, pin_memory, compute_device, readback_to_cpu)
         k, n = t.element_size(), t.numel()
         if n * k < min_compress_bytes or n == 0:
-            blobs[i] = compress_tensor(t, chunk_bytes=chunk_bytes, sub_chunk_bytes=sub_chunk_bytes,
-                                       passthrough_threshold=passthrough_threshold,
-                                       min_compress_bytes=min_compress_bytes, pin_memory=pin_memory,
-                                       compute_device=compute_device, readback_to_cpu=readback_to_cpu)
+            small.append(i)
         else:
             groups.setdefault((k, t.dtype in _REORDER), []).append(i)
+
+    def compress_small(device: torch.device | None) -> None:
+        batch = []
+        for i in small:
+            t = tensors[i]
+            k, n = t.element_size(), t.numel()
+            if (device is not None and not readback_to_cpu and n * k <= _COPY_BATCH_MAX
+                    and _gpu(t.detach(), _check_device(compute_device)) == device):
+                stored = n * k < min_compress_bytes
+                flags = _FLAG_STORED if stored else _FLAG_REORDER if t.dtype in _REORDER else 0
+                batch.append((i, t.detach(), _header(t, flags, 0 if stored else chunk_bytes, 0)))
+            else:
+                blobs[i] = compress_tensor(t, chunk_bytes=chunk_bytes, sub_chunk_bytes=sub_chunk_bytes,
+                                           passthrough_threshold=passthrough_threshold,
+                                           min_compress_bytes=min_compress_bytes, pin_memory=pin_memory,
+                                           compute_device=compute_device, readback_to_cpu=readback_to_cpu)
+        if batch:
+            for i, b in _stored_blobs_gpu(batch, device).items():
+                blobs[i] = b
+
     if not groups:
+        if small and not readback_to_cpu:
+            device = _gpu(tensors[small[0]].detach(), _check_device(compute_device))
+            with torch.cuda.device(device):
+                compress_small(device)
+        else:
+            compress_small(None)
         return blobs  # type: ignore[return-value]
     first = tensors[next(iter(groups.values()))[0]]
     device = _gpu(first.detach(), _check_device(compute_device))
@@ -541,6 +614,8 @@ def compress_tensors(
                 "zn_compress_batch",
             )
             pending.append((idx, out, offs, sizes, xs, temp))
+        # The small tensors' host work overlaps the coded kernels.
+        compress_small(device)
         all_sizes = torch.cat([p[3] for p in pending]).cpu().tolist()  # the one synchronization
         pos = 0
         for idx, out, offs, _, _, _ in pending:
@@ -572,6 +647,34 @@ def decompress_tensors(
     for blob in blobs:
         if blob.dtype != torch.uint8 or blob.dim() != 1:
             raise ValueError("blob must be a 1-D uint8 tensor")
+    small: list[tuple[int, torch.dtype, tuple[int, ...], int]] = []  # stored / empty, after the launches
+
+    def decompress_small() -> None:
+        """Stored blobs on the GPU decode into GPU tensors by one batched copy; the rest (CPU blobs,
+        CPU outputs, empty tensors) take decompress_tensor."""
+        srcs, dsts, sizes = [], [], []
+        bdev = None  # the one device whose stored blobs are batched
+        for i, dtype, shape, flags in small:
+            b = blobs[i].detach()
+            header_size = _FIXED.size + 8 * len(shape)
+            nbytes = math.prod(shape) * dtype.itemsize
+            if (flags & _FLAG_STORED and b.is_cuda and not readback_to_cpu and 0 < nbytes <= _COPY_BATCH_MAX
+                    and (b.data_ptr() + header_size) % 8 == 0 and _gpu(b, compute_device) == b.device
+                    and bdev in (None, b.device)):
+                bdev = b.device
+                if b.numel() < header_size + nbytes:
+                    raise ValueError("blob is truncated")
+                y = torch.empty(shape, dtype=dtype, device=b.device)
+                srcs.append(b.data_ptr() + header_size)
+                dsts.append(y.data_ptr())
+                sizes.append(nbytes)
+                outs[i] = y
+            else:
+                outs[i] = decompress_tensor(b, compute_device=compute_device, readback_to_cpu=readback_to_cpu)
+        if srcs:
+            with torch.cuda.device(bdev):
+                _copy_batch(bdev, srcs, dsts, sizes)
+
     # Headers of GPU blobs come to the host in one copy per device.
     plen = [min(b.numel(), _FIXED.size + 8 * _MAX_NDIM) for b in blobs]
     prefixes: list[torch.Tensor | None] = [None] * len(blobs)
@@ -594,7 +697,7 @@ def decompress_tensors(
             (ctypes.c_byte * plen[i]).from_address(pre.data_ptr())
         )
         if flags & _FLAG_STORED or n == 0:
-            outs[i] = decompress_tensor(blob, compute_device=compute_device, readback_to_cpu=readback_to_cpu)
+            small.append((i, dtype, shape, flags))
             continue
         if math.prod(shape) != n or chunk_bytes <= 0:
             raise ValueError("not a cuzipnn blob")
@@ -607,6 +710,7 @@ def decompress_tensors(
             (i, (dtype, shape, chunk_bytes, n_comp, n))
         )
     if not groups:
+        decompress_small()
         return outs  # type: ignore[return-value]
     first = blobs[next(iter(groups.values()))[0][0]]
     device = _gpu(first, compute_device)
@@ -647,6 +751,7 @@ def decompress_tensors(
             _LAST_STATUS[device.index] = status
             for (i, _), y in zip(items, ys):
                 outs[i] = y
+        decompress_small()
         for ev in uploaded:
             ev.synchronize()
         if readback_to_cpu:

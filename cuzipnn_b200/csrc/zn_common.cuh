@@ -201,17 +201,33 @@ __device__ __forceinline__ void store_words(uint8_t* p, const uint32_t* w, int n
   }
 }
 
-// Index of the job whose chunk range holds global chunk `gchunk` (jobs sorted by chunk0; a job
-// without chunks never matches because the next job starts at the same chunk0).
+// A batch's job table in device memory: njobs structs, then (for more than one job) a map from
+// global chunk index to job index, so that a CTA finds its job with one load instead of a binary
+// search through the job structs (a chain of dependent loads at the start of every CTA).
+template <class J>
+__host__ __device__ constexpr size_t job_structs_bytes(int njobs) {
+  return (size_t(njobs) * sizeof(J) + 255) & ~size_t(255);
+}
+template <class J>
+__host__ __device__ constexpr size_t job_table_bytes(int njobs, int64_t total_chunks) {
+  return job_structs_bytes<J>(njobs) + (njobs > 1 ? (size_t(total_chunks) * 4 + 255) & ~size_t(255) : 0);
+}
+
+// Index of the job whose chunk range holds global chunk `gchunk`.
 template <class J>
 __device__ __forceinline__ int find_job(const J* __restrict__ jobs, int njobs, int64_t gchunk) {
-  int lo = 0, hi = njobs - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (jobs[mid].chunk0 <= gchunk) lo = mid;
-    else hi = mid - 1;
-  }
-  return lo;
+  if (njobs == 1) return 0;
+  const int32_t* map = reinterpret_cast<const int32_t*>(reinterpret_cast<const uint8_t*>(jobs) + job_structs_bytes<J>(njobs));
+  return __ldg(map + gchunk);
+}
+
+// Fill the chunk -> job map: CTA i writes i over job i's chunk range [chunk0_i, chunk0_{i+1}).
+template <class J>
+__global__ void map_jobs_kernel(const J* __restrict__ jobs, int njobs, int64_t total_chunks) {
+  int32_t* map = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(const_cast<J*>(jobs)) + job_structs_bytes<J>(njobs));
+  const int i = blockIdx.x;
+  const int64_t c0 = jobs[i].chunk0, c1 = i + 1 < njobs ? jobs[i + 1].chunk0 : total_chunks;
+  for (int64_t c = c0 + threadIdx.x; c < c1; c += blockDim.x) map[c] = i;
 }
 
 // Job tables reach device memory as kernel parameters (copied by the launch itself), so no host
@@ -238,9 +254,10 @@ int check_launch(const char* what);
 void count_launch(int n = 1);
 int set_max_smem(const void* func, int bytes);
 
-// Copy `count` host structs to device memory at dev, on stream s, through kernel parameters.
+// Copy `count` host structs to device memory at dev, on stream s, through kernel parameters, and
+// (for more than one job) build the chunk -> job map behind them (job_table_bytes).
 template <class T>
-int upload_jobs(const T* host, int count, T* dev, cudaStream_t s) {
+int upload_jobs(const T* host, int count, T* dev, int64_t total_chunks, cudaStream_t s) {
   constexpr int N = 30000 / int(sizeof(T)) > 0 ? 30000 / int(sizeof(T)) : 1;
   for (int i = 0; i < count; i += N) {
     UploadBatch<T, N> b;
@@ -249,6 +266,11 @@ int upload_jobs(const T* host, int count, T* dev, cudaStream_t s) {
     upload_kernel<T, N><<<1, 256, 0, s>>>(b, dev + i);
     count_launch();
     if (int rc = check_launch("upload_kernel")) return rc;
+  }
+  if (count > 1 && total_chunks > 0) {
+    map_jobs_kernel<T><<<unsigned(count), 256, 0, s>>>(dev, count, total_chunks);
+    count_launch();
+    if (int rc = check_launch("map_jobs_kernel")) return rc;
   }
   return ZN_OK;
 }

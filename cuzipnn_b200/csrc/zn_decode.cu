@@ -253,6 +253,36 @@ __device__ __forceinline__ void decode_round(Cursor* cb, const uint32_t* __restr
   }
 }
 
+// Raw (stored) plane bytes of round r for each chain: 16 bytes per plane from the lane's 16
+// symbols, byte by byte in a partial last round.  Coded planes are left untouched.
+template <int K, int NC>
+__device__ __forceinline__ void load_raw_round(const uint8_t* const* src, const bool* coded, const int64_t* base,
+                                               const int64_t* len, int r, int l, uint32_t (*p)[K][4]) {
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int64_t off = int64_t(r) * kRound + l * kSteps;
+    const int nact = int(max(int64_t(0), min(int64_t(kSteps), len[c] - off)));
+#pragma unroll
+    for (int b = 0; b < K; ++b) {
+      if (coded[b]) continue;
+      const uint8_t* sp = src[b] + base[c] + off;
+      if (nact == 16) {
+        const uint2 v0 = reinterpret_cast<const uint2*>(sp)[0], v1 = reinterpret_cast<const uint2*>(sp)[1];
+        p[c][b][0] = v0.x; p[c][b][1] = v0.y; p[c][b][2] = v1.x; p[c][b][3] = v1.y;
+      } else {
+        uint64_t vlo = 0, vhi = 0;
+        for (int i = 0; i < nact; ++i) {
+          const uint64_t byte = sp[i];
+          if (i < 8) vlo |= byte << (8 * i);
+          else vhi |= byte << (8 * (i - 8));
+        }
+        p[c][b][0] = uint32_t(vlo); p[c][b][1] = uint32_t(vlo >> 32);
+        p[c][b][2] = uint32_t(vhi); p[c][b][3] = uint32_t(vhi >> 32);
+      }
+    }
+  }
+}
+
 // KC: coded planes per chunk held in shared memory.  The main pass (KC = 1 for K > 1) flags
 // chunks with more coded planes; a second pass with KC = K decodes only those.
 // Work split: a warp item is 8 sub-chunks; lane l of 8-lane segment g runs chain c on sub-chunk
@@ -397,6 +427,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
           err |= cb.x < kL;
         }
       }
+    uint32_t pn[kChains][K][4];
+    load_raw_round<K, kChains>(src, coded, base, len, 0, l, pn);
     for (int r = 0; r < rounds; ++r) {
       int nact[kChains];
       int64_t off[kChains];
@@ -425,27 +457,16 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
           if (cb.nload > 1) cb.r1 = load_block(gb[q], cb.fill / 8 + 1, lo[q], hi[q]);
         }
       }
+      // This round's raw-plane bytes were loaded during the previous round; start the next
+      // round's loads now, so that they overlap this round's decoding.
       uint32_t p[kChains][K][4];
 #pragma unroll
       for (int c = 0; c < kChains; ++c)
 #pragma unroll
-        for (int b = 0; b < K; ++b) {
-          if (coded[b]) continue;
-          const uint8_t* sp = src[b] + base[c] + off[c];
-          if (nact[c] == 16) {
-            const uint2 v0 = reinterpret_cast<const uint2*>(sp)[0], v1 = reinterpret_cast<const uint2*>(sp)[1];
-            p[c][b][0] = v0.x; p[c][b][1] = v0.y; p[c][b][2] = v1.x; p[c][b][3] = v1.y;
-          } else {
-            uint64_t vlo = 0, vhi = 0;
-            for (int i = 0; i < nact[c]; ++i) {
-              const uint64_t byte = sp[i];
-              if (i < 8) vlo |= byte << (8 * i);
-              else vhi |= byte << (8 * (i - 8));
-            }
-            p[c][b][0] = uint32_t(vlo); p[c][b][1] = uint32_t(vlo >> 32);
-            p[c][b][2] = uint32_t(vhi); p[c][b][3] = uint32_t(vhi >> 32);
-          }
-        }
+        for (int b = 0; b < K; ++b)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) p[c][b][i] = pn[c][b][i];
+      if (r + 1 < rounds) load_raw_round<K, kChains>(src, coded, base, len, r + 1, l, pn);
       const bool full = nact[0] == kSteps && nact[kChains - 1] == kSteps;
 #pragma unroll
       for (int q = 0; q < KC; ++q) {
@@ -597,7 +618,6 @@ int launch_decode(const DecArgs* jobs, int njobs, int64_t grid, cudaStream_t s) 
   return ZN_OK;
 }
 
-size_t dec_table_bytes(int njobs) { return (size_t(njobs) * sizeof(DecArgs) + 255) & ~size_t(255); }
 size_t dec_job_bytes(int64_t n, int k, int64_t chunk_bytes) {
   const int64_t nch = cdiv(n, chunk_bytes);
   return (size_t(int64_t(k) * nch) * 8 + size_t(nch) + 255) & ~size_t(255);  // unit offsets, overflow flags
@@ -610,13 +630,13 @@ using namespace zn;
 
 extern "C" {
 
-size_t zn_ans_decompress_temp_bytes(int64_t count) { (void)count; return dec_table_bytes(1); }
+size_t zn_ans_decompress_temp_bytes(int64_t count) { return job_table_bytes<DecArgs>(1, count); }
 
 int zn_ans_decompress(const int64_t* in_ptrs, const int64_t* in_bytes, const int64_t* out_capacity, int64_t count,
                       const int64_t* out_ptrs, int32_t* statuses, void* temp, size_t temp_bytes, void* stream) {
   if (count < 0 || count > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_ans_decompress: bad arguments");
   if (count == 0) return ZN_OK;
-  if (!temp || temp_bytes < dec_table_bytes(1)) return set_error(ZN_ERR_SPACE, "zn_ans_decompress: temp buffer too small");
+  if (!temp || temp_bytes < job_table_bytes<DecArgs>(1, count)) return set_error(ZN_ERR_SPACE, "zn_ans_decompress: temp buffer too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   DecArgs a{};
   a.in_ptrs = in_ptrs;
@@ -626,18 +646,20 @@ int zn_ans_decompress(const int64_t* in_ptrs, const int64_t* in_bytes, const int
   a.statuses = statuses;
   a.nch = count;
   DecArgs* dj = static_cast<DecArgs*>(temp);
-  if (int rc = upload_jobs(&a, 1, dj, s)) return rc;
+  if (int rc = upload_jobs(&a, 1, dj, count, s)) return rc;
   return launch_decode<1, false>(dj, 1, count, s);
 }
 
 size_t zn_decompress_batch_temp_bytes(int njobs, const int64_t* n, int k, const int64_t* chunk_bytes) {
   if (njobs < 0 || k <= 0) return 0;
-  size_t total = dec_table_bytes(njobs);
+  size_t total = 0;
+  int64_t chunks = 0;
   for (int i = 0; i < njobs; ++i) {
     if (n[i] < 0 || chunk_bytes[i] <= 0) return 0;
+    chunks += cdiv(n[i], chunk_bytes[i]);
     total += dec_job_bytes(n[i], k, chunk_bytes[i]);
   }
-  return total;
+  return total + job_table_bytes<DecArgs>(njobs, chunks);
 }
 
 size_t zn_decompress_temp_bytes(int64_t n, int k, int64_t chunk_bytes) {
@@ -654,7 +676,9 @@ int zn_decompress_batch(int njobs, const void* const* blobs, const int64_t* blob
     return set_error(ZN_ERR_SPACE, "zn_decompress: temp buffer too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* tb = static_cast<uint8_t*>(temp);
-  uint8_t* region = tb + dec_table_bytes(njobs);
+  int64_t total_chunks = 0;
+  for (int i = 0; i < njobs; ++i) total_chunks += n[i] > 0 && chunk_bytes[i] > 0 ? cdiv(n[i], chunk_bytes[i]) : 0;
+  uint8_t* region = tb + job_table_bytes<DecArgs>(njobs, total_chunks);
   std::vector<DecArgs> jobs;
   jobs.reserve(static_cast<size_t>(njobs));
   int64_t chunk0 = 0;
@@ -689,7 +713,7 @@ int zn_decompress_batch(int njobs, const void* const* blobs, const int64_t* blob
   if (nj == 0) return ZN_OK;
   if (chunk0 > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_decompress: too many chunks");
   DecArgs* dj = reinterpret_cast<DecArgs*>(tb);
-  if (int rc = upload_jobs(jobs.data(), nj, dj, s)) return rc;
+  if (int rc = upload_jobs(jobs.data(), nj, dj, chunk0, s)) return rc;
   {
     TimedLaunch tl("dscan", s);
     dscan_kernel<<<unsigned(nj), kScanThreads, 0, s>>>(dj);

@@ -660,31 +660,51 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const EncArgs* __res
 
 constexpr int kPackThreads = 256;
 
+// Present symbols of a payload: the popcount of its bitmap, bytes [2, 34) of the 16-byte aligned
+// meta block, read as three 16-byte loads.
 __device__ __forceinline__ int count_present(const uint8_t* meta) {
-  int np = 0;
-  for (int q = 0; q < 32; ++q) np += __popc(uint32_t(meta[2 + q]));
-  return np;
+  const uint4* m4 = reinterpret_cast<const uint4*>(meta);
+  const uint4 a = m4[0], b = m4[1], c = m4[2];
+  return __popc(a.x >> 16) + __popc(a.y) + __popc(a.z) + __popc(a.w) + __popc(b.x) + __popc(b.y) + __popc(b.z) +
+         __popc(b.w) + __popc(c.x & 0xFFFFu);
 }
 
-// Copy halfwords [h0, h1) of one coded payload (the meta block, then the sub-chunk streams from
-// the tails of their scratch slots) to dst, which is 2-byte aligned.  Threads of the CTA stride
-// over the range with kCopyDepth loads in flight.
-constexpr int kCopyDepth = 4;
-
-__device__ __forceinline__ void copy_halfwords(uint16_t* dst, const uint16_t* src, int64_t n) {
-  for (int64_t i0 = threadIdx.x; i0 < n; i0 += kCopyDepth * int64_t(blockDim.x)) {
-    uint16_t v[kCopyDepth];
-#pragma unroll
-    for (int d = 0; d < kCopyDepth; ++d) {
-      const int64_t i = i0 + d * int64_t(blockDim.x);
-      if (i < n) v[d] = src[i];
-    }
-#pragma unroll
-    for (int d = 0; d < kCopyDepth; ++d) {
-      const int64_t i = i0 + d * int64_t(blockDim.x);
-      if (i < n) dst[i] = v[d];
-    }
+// Warp-cooperative copy of L bytes (L even) from src to dst, both 2-byte aligned.  Each 16-byte
+// aligned block of dst is assembled from the two aligned 16-byte source blocks it straddles (a
+// funnel shift by their relative offset), so the body moves with 16-byte loads and stores; the
+// ragged head and tail (under 16 bytes each) move by halfwords.  The source loads stay inside the
+// 16-byte aligned span that holds the source bytes.
+__device__ __forceinline__ uint4 shift_blocks(const uint4& A, const uint4& B, uint32_t q, uint32_t sh) {
+  const uint32_t w0 = A.x, w1 = A.y, w2 = A.z, w3 = A.w, w4 = B.x, w5 = B.y, w6 = B.z, w7 = B.w;
+  switch (q) {
+    case 0: return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
+                              __funnelshift_r(w3, w4, sh));
+    case 1: return make_uint4(__funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh), __funnelshift_r(w3, w4, sh),
+                              __funnelshift_r(w4, w5, sh));
+    case 2: return make_uint4(__funnelshift_r(w2, w3, sh), __funnelshift_r(w3, w4, sh), __funnelshift_r(w4, w5, sh),
+                              __funnelshift_r(w5, w6, sh));
+    default: return make_uint4(__funnelshift_r(w3, w4, sh), __funnelshift_r(w4, w5, sh), __funnelshift_r(w5, w6, sh),
+                               __funnelshift_r(w6, w7, sh));
   }
+}
+
+__device__ __forceinline__ void warp_copy16(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, int64_t L,
+                                            int lane) {
+  const int64_t h = min(L, int64_t((16 - (reinterpret_cast<uintptr_t>(dst) & 15)) & 15));
+  if (2 * lane < h) reinterpret_cast<uint16_t*>(dst)[lane] = reinterpret_cast<const uint16_t*>(src)[lane];
+  const int64_t nb = (L - h) >> 4;
+  const uint8_t* s = src + h;
+  const uint32_t r = uint32_t(reinterpret_cast<uintptr_t>(s) & 15);
+  const uint4* sa = reinterpret_cast<const uint4*>(s - r);
+  uint4* d = reinterpret_cast<uint4*>(dst + h);
+  const uint32_t q = r >> 2, sh = (r & 3) * 8;
+  for (int64_t k = lane; k < nb; k += 32) {
+    const uint4 A = sa[k];
+    d[k] = r ? shift_blocks(A, sa[k + 1], q, sh) : A;
+  }
+  const int64_t t0 = h + nb * 16;
+  if (2 * lane < L - t0)
+    reinterpret_cast<uint16_t*>(dst + t0)[lane] = reinterpret_cast<const uint16_t*>(src + t0)[lane];
 }
 
 // Exclusive prefix sums of the nu * 8 stream lengths of a payload into pre[] (shared), by all
@@ -715,30 +735,32 @@ __device__ void stream_prefix(const uint8_t* meta, int64_t tb, const Geom& g, in
   __syncthreads();
 }
 
-// Copy part `part` of `nparts` of one coded payload to dst (2-byte aligned): the meta block (part
-// 0), then its share of the nu * 8 streams, each from the tail of its slot, one warp per stream.
-// Called by all threads of the CTA.
+// Copy part `part` of `nparts` of one coded payload to dst (8-byte aligned): the meta block (part
+// 0), then its share of the nu * 8 streams, each from the tail of its scratch slot to its place
+// after the meta block (from the prefix sums of the stream lengths).  One warp per item.  Called
+// by all threads of the CTA.
 __device__ void copy_payload(const EncArgs& a, uint64_t u, int64_t m, uint8_t* dst, int npres, int part, int nparts,
                              int32_t* pre, int32_t* warp_tot) {
   const uint8_t* meta = a.meta + u * a.meta_slot;
   const Geom g = geom_of(m, a.t);
   const int64_t tb = table_bytes(npres);
   const int64_t mh = meta_bytes(npres, g) / 2;
-  uint16_t* d16 = reinterpret_cast<uint16_t*>(dst);
-  if (part == 0) copy_halfwords(d16, reinterpret_cast<const uint16_t*>(meta), mh);
   stream_prefix(meta, tb, g, pre, warp_tot);
   const int S = g.nu * kLanes;
   const int f0 = int(int64_t(S) * part / nparts), f1 = int(int64_t(S) * (part + 1) / nparts);
-  const int lane = threadIdx.x & 31, nwarps = blockDim.x / 32;
-  for (int fi = f0 + int(threadIdx.x >> 5); fi < f1; fi += nwarps) {
-    const int gi = fi / kLanes, l = fi % kLanes;
-    const int32_t n = fi + 1 < S ? pre[fi + 1] - pre[fi]
-                      : (g.lw == 2 ? int32_t(reinterpret_cast<const uint16_t*>(meta + tb)[fi])
-                                   : int32_t(reinterpret_cast<const uint32_t*>(meta + tb)[fi]));
-    const uint16_t* src = a.streams + u * a.unit_words + int64_t(gi) * a.sub_words + int64_t(l) * a.lane_words +
-                          (a.lane_words - n);
-    uint16_t* d = d16 + mh + pre[fi];
-    for (int i = lane; i < n; i += 32) d[i] = src[i];
+  const int lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const uint16_t* streams = a.streams + u * a.unit_words;
+  for (int it = f0 - (part == 0) + int(threadIdx.x >> 5); it < f1; it += nwarps) {
+    if (it < f0) {  // the meta block (table, lengths, states)
+      warp_copy16(dst, meta, 2 * mh, lane);
+      continue;
+    }
+    const int32_t n = it + 1 < S ? pre[it + 1] - pre[it]
+                      : (g.lw == 2 ? int32_t(reinterpret_cast<const uint16_t*>(meta + tb)[it])
+                                   : int32_t(reinterpret_cast<const uint32_t*>(meta + tb)[it]));
+    const int gi = it / kLanes, l = it % kLanes;
+    const uint16_t* src = streams + int64_t(gi) * a.sub_words + int64_t(l) * a.lane_words + (a.lane_words - n);
+    warp_copy16(dst + 2 * (mh + int64_t(pre[it])), reinterpret_cast<const uint8_t*>(src), 2 * int64_t(n), lane);
   }
   __syncthreads();
 }
@@ -747,9 +769,11 @@ __device__ void copy_payload(const EncArgs& a, uint64_t u, int64_t m, uint8_t* d
 // chunk's elements for the raw planes.  Chunks run in reverse order, so the most recently encoded
 // (and read) chunks are still in L2.
 constexpr int kPackParts = 8;
+template <int K>
+constexpr int kPackGroups = K >= 4 ? 1 : 4 / K;
 
 template <int K, bool REORDER>
-__global__ void __launch_bounds__(kPackThreads) pack_kernel(const EncArgs* __restrict__ jobs, int njobs, int64_t total_chunks) {
+__global__ void __launch_bounds__(kPackThreads, 4) pack_kernel(const EncArgs* __restrict__ jobs, int njobs, int64_t total_chunks) {
   __shared__ int32_t pre[512];
   __shared__ int32_t warp_tot[kPackThreads / 32];
   const int64_t gj = total_chunks - 1 - blockIdx.x;
@@ -761,12 +785,11 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const EncArgs* __res
   __shared__ int npres[K];
   uint8_t* dst[K];
   bool coded[K];
-  bool any_raw = false;
-  if (threadIdx.x < K) {
+  bool any_raw = false, any_coded = false;
+  if (part == 0 && threadIdx.x < K) {
     const uint64_t u = uint64_t(threadIdx.x) * a.nch + j;
     npres[threadIdx.x] = (a.dst_rel[u] >> 62) & 1 ? count_present(a.meta + u * a.meta_slot) : 0;
   }
-  __syncthreads();
 #pragma unroll
   for (int b = 0; b < K; ++b) {
     const uint64_t u = uint64_t(b) * a.nch + j;
@@ -774,29 +797,48 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const EncArgs* __res
     coded[b] = (d >> 62) & 1;
     dst[b] = a.out + data_off + (d & ((int64_t(1) << 62) - 1));
     any_raw |= !coded[b];
-    if (coded[b]) {
-      const int64_t size = a.comp_bytes[u];
-      copy_payload(a, u, m, dst[b], npres[b], part, kPackParts, pre, warp_tot);
-      if (part == kPackParts - 1 && threadIdx.x < 8 && size + threadIdx.x < align8(size)) dst[b][size + threadIdx.x] = 0;
-    }
+    any_coded |= coded[b];
   }
-  if (!any_raw) return;
+  // Raw planes: this part's 16-element groups, kPackGroups per thread per pass (128 input bytes).
+  // The first pass's loads are issued before the payload copy so that the two overlap.
+  constexpr int G = kPackGroups<K>;
   const uint8_t* xc = a.x + j * a.C * K;
   const uintptr_t xa = reinterpret_cast<uintptr_t>(xc);
   const int mode = (xa & 15) == 0 ? 2 : (xa & 7) == 0 ? 1 : 0;
-  const int64_t ngrp = mode ? m / 16 : 0;
+  const int64_t ngrp = (mode && any_raw) ? m / 16 : 0;
   const int64_t gper = cdiv(ngrp, kPackParts);
   const int64_t g0 = part * gper, g1 = min(ngrp, g0 + gper);
-  for (int64_t v0 = g0 + threadIdx.x; v0 < g1; v0 += 2 * kPackThreads) {
-    uint32_t e[2][4 * K];
+  uint32_t e[G][4 * K];
+  int64_t vb = g0 + threadIdx.x;
 #pragma unroll
-    for (int d = 0; d < 2; ++d) {
-      const int64_t v = v0 + d * kPackThreads;
-      if (v < g1) load_words(xc + v * 16 * K, e[d], 4 * K, mode == 2);
+  for (int d = 0; d < G; ++d) {
+    const int64_t v = vb + d * kPackThreads;
+    if (v < g1) load_words(xc + v * 16 * K, e[d], 4 * K, mode == 2);
+  }
+  // Coded payloads: part 0 copies them whole (one prefix computation per payload).
+  if (any_coded && part == 0) {
+    __syncthreads();  // npres
+#pragma unroll
+    for (int b = 0; b < K; ++b) {
+      if (!coded[b]) continue;
+      const uint64_t u = uint64_t(b) * a.nch + j;
+      const int64_t size = a.comp_bytes[u];
+      copy_payload(a, u, m, dst[b], npres[b], 0, 1, pre, warp_tot);
+      if (threadIdx.x < 8 && size + threadIdx.x < align8(size)) dst[b][size + threadIdx.x] = 0;
+    }
+  }
+  if (!any_raw) return;
+  for (; vb < g1; vb += G * kPackThreads) {
+    if (vb != g0 + threadIdx.x) {
+#pragma unroll
+      for (int d = 0; d < G; ++d) {
+        const int64_t v = vb + d * kPackThreads;
+        if (v < g1) load_words(xc + v * 16 * K, e[d], 4 * K, mode == 2);
+      }
     }
 #pragma unroll
-    for (int d = 0; d < 2; ++d) {
-      const int64_t v = v0 + d * kPackThreads;
+    for (int d = 0; d < G; ++d) {
+      const int64_t v = vb + d * kPackThreads;
       if (v >= g1) break;
       reorder_words<K, REORDER, true>(e[d], 4 * K);
       uint32_t p[K][4];
@@ -814,11 +856,11 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const EncArgs* __res
     }
   }
   if (part != kPackParts - 1) return;
-  for (int64_t e = ngrp * 16 + threadIdx.x; e < m; e += kPackThreads) {
-    const uint64_t w = reorder_elem<K, REORDER>(load_elem<K>(xc + e * K));
+  for (int64_t e1 = (mode ? m / 16 : 0) * 16 + threadIdx.x; e1 < m; e1 += kPackThreads) {
+    const uint64_t w = reorder_elem<K, REORDER>(load_elem<K>(xc + e1 * K));
 #pragma unroll
     for (int b = 0; b < K; ++b)
-      if (!coded[b]) dst[b][e] = uint8_t(w >> (8 * b));
+      if (!coded[b]) dst[b][e1] = uint8_t(w >> (8 * b));
   }
   if (threadIdx.x < 8 && m + threadIdx.x < align8(m)) {
 #pragma unroll
@@ -880,7 +922,6 @@ EncLayout enc_layout(int64_t units, int64_t C, int t) {
 size_t enc_smem(int K) { return size_t(K) * 256 * 16 + sizeof(EncSmem); }
 size_t hist_smem(int K) { return size_t(K) * 256 * kCols * 4; }
 
-size_t job_table_bytes(int njobs) { return (size_t(njobs) * sizeof(EncArgs) + 255) & ~size_t(255); }
 
 int sub_log2(int sub_chunks) {
   for (int t = kMinSubLog2; t <= kMaxSubLog2; ++t)
@@ -950,7 +991,7 @@ int64_t zn_ans_max_compressed_chunk_bytes(int64_t chunk_bytes, int sub_chunks) {
 size_t zn_ans_compress_temp_bytes(int64_t count, int64_t chunk_bytes, int sub_chunks) {
   const int t = sub_log2(sub_chunks);
   if (t < 0 || count < 0 || chunk_bytes <= 0) return 0;
-  return job_table_bytes(1) + enc_layout(count, chunk_bytes, t).total;
+  return job_table_bytes<EncArgs>(1, count) + enc_layout(count, chunk_bytes, t).total;
 }
 
 int zn_ans_compress(const int64_t* in_ptrs, const int64_t* in_bytes, int64_t chunk_bytes, int64_t count,
@@ -972,9 +1013,9 @@ int zn_ans_compress(const int64_t* in_ptrs, const int64_t* in_bytes, int64_t chu
   a.t = t;
   a.allow_skip = 0;
   a.threshold = 1.0;
-  bind_scratch(a, tb + job_table_bytes(1), count);
+  bind_scratch(a, tb + job_table_bytes<EncArgs>(1, count), count);
   EncArgs* dj = reinterpret_cast<EncArgs*>(tb);
-  if (int rc = upload_jobs(&a, 1, dj, s)) return rc;
+  if (int rc = upload_jobs(&a, 1, dj, count, s)) return rc;
   if (int rc = launch_encode<1, false>(dj, 1, count, s)) return rc;
   assemble_kernel<<<unsigned(count), kPackThreads, 0, s>>>(dj, in_bytes, out_ptrs, out_bytes, statuses);
   count_launch();
@@ -992,12 +1033,14 @@ int64_t zn_compress_bound(int64_t n, int k, int ndim, int64_t chunk_bytes) {
 size_t zn_compress_batch_temp_bytes(int njobs, const int64_t* n, int k, int64_t chunk_bytes, int sub_chunks) {
   const int t = sub_log2(sub_chunks);
   if (t < 0 || njobs < 0 || k <= 0 || chunk_bytes <= 0) return 0;
-  size_t total = job_table_bytes(njobs);
+  size_t total = 0;
+  int64_t chunks = 0;
   for (int i = 0; i < njobs; ++i) {
     if (n[i] < 0) return 0;
+    chunks += cdiv(n[i], chunk_bytes);
     total += enc_layout(int64_t(k) * cdiv(n[i], chunk_bytes), chunk_bytes, t).total;
   }
-  return total;
+  return total + job_table_bytes<EncArgs>(njobs, chunks);
 }
 
 size_t zn_compress_temp_bytes(int64_t n, int k, int64_t chunk_bytes, int sub_chunks) {
@@ -1016,7 +1059,9 @@ int zn_compress_batch(int njobs, const void* const* x, const int64_t* n, int k, 
     return set_error(ZN_ERR_SPACE, "zn_compress: temp buffer too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* tb = static_cast<uint8_t*>(temp);
-  uint8_t* region = tb + job_table_bytes(njobs);
+  int64_t total_chunks = 0;
+  for (int i = 0; i < njobs; ++i) total_chunks += cdiv(n[i], chunk_bytes);
+  uint8_t* region = tb + job_table_bytes<EncArgs>(njobs, total_chunks);
   std::vector<EncArgs> jobs(static_cast<size_t>(njobs));
   int64_t chunk0 = 0;
   for (int i = 0; i < njobs; ++i) {
@@ -1049,7 +1094,7 @@ int zn_compress_batch(int njobs, const void* const* x, const int64_t* n, int k, 
   }
   if (chunk0 > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_compress: too many chunks");
   EncArgs* dj = reinterpret_cast<EncArgs*>(tb);
-  if (int rc = upload_jobs(jobs.data(), njobs, dj, s)) return rc;
+  if (int rc = upload_jobs(jobs.data(), njobs, dj, chunk0, s)) return rc;
   int rc = ZN_OK;
   switch (k * 2 + (reorder ? 1 : 0)) {
     case 2: rc = launch_encode<1, false>(dj, njobs, chunk0, s); break;
