@@ -63,7 +63,7 @@ struct EncArgs {
 
 // Parts per chunk of the histogram kernel: a chunk's histogram is built by kHistParts CTAs, so
 // the chunk is read at the full memory bandwidth rather than by one CTA.
-constexpr int kHistParts = 8;
+constexpr int kHistParts = 2;
 constexpr int kHistThreads = 256;
 
 struct EncSmem {
@@ -185,24 +185,42 @@ __device__ __forceinline__ void plane_symbols(const uint8_t* xc, int64_t e0, int
 constexpr int kHistDepth = 4;
 
 template <int K, bool REORDER, int VB>
+__device__ __forceinline__ void hist_count(uint32_t (&w)[VB / 4], uint32_t* hist, int col) {
+  reorder_words<K, REORDER, true>(w, VB / 4);
+#pragma unroll
+  for (int q = 0; q < VB; ++q) {
+    const uint32_t byte = (w[q >> 2] >> (8 * (q & 3))) & 0xFF;
+    atomicAdd(&hist[(((q % K) << 8) | byte) * kCols + col], 1u);
+  }
+}
+
+// Count the VB-byte vectors of xc[0, m * K): kHistDepth vectors per thread per batch, the next
+// batch's loads issued before the current batch is counted.  Returns the elements covered.
+template <int K, bool REORDER, int VB>
 __device__ __forceinline__ int64_t hist_vectors(const uint8_t* xc, int64_t m, uint32_t* hist, int col) {
   const int64_t nvec = m * K / VB;
-  for (int64_t v0 = threadIdx.x; v0 < nvec; v0 += kHistDepth * int64_t(blockDim.x)) {
-    uint32_t w[kHistDepth][VB / 4];
+  const int64_t step = kHistDepth * int64_t(blockDim.x);
+  uint32_t w[kHistDepth][VB / 4], nx[kHistDepth][VB / 4];
+  int64_t v0 = threadIdx.x;
+#pragma unroll
+  for (int d = 0; d < kHistDepth; ++d) {
+    const int64_t v = v0 + d * int64_t(blockDim.x);
+    if (v < nvec) load_words(xc + v * VB, nx[d], VB / 4, VB == 16);
+  }
+  for (; v0 < nvec; v0 += step) {
+#pragma unroll
+    for (int d = 0; d < kHistDepth; ++d)
+#pragma unroll
+      for (int i = 0; i < VB / 4; ++i) w[d][i] = nx[d][i];
 #pragma unroll
     for (int d = 0; d < kHistDepth; ++d) {
-      const int64_t v = v0 + d * int64_t(blockDim.x);
-      if (v < nvec) load_words(xc + v * VB, w[d], VB / 4, VB == 16);
+      const int64_t v = v0 + step + d * int64_t(blockDim.x);
+      if (v < nvec) load_words(xc + v * VB, nx[d], VB / 4, VB == 16);
     }
 #pragma unroll
     for (int d = 0; d < kHistDepth; ++d) {
       if (v0 + d * int64_t(blockDim.x) >= nvec) break;
-      reorder_words<K, REORDER, true>(w[d], VB / 4);
-#pragma unroll
-      for (int q = 0; q < VB; ++q) {
-        const uint32_t byte = (w[d][q >> 2] >> (8 * (q & 3))) & 0xFF;
-        atomicAdd(&hist[(((q % K) << 8) | byte) * kCols + col], 1u);
-      }
+      hist_count<K, REORDER, VB>(w[d], hist, col);
     }
   }
   return nvec * VB / K;
