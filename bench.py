@@ -358,6 +358,27 @@ def main() -> None:
     one_c = max_over_ranks(min(v[0] for v in ev1)) if ev1 else None
     one_d = max_over_ranks(min(v[1] for v in ev1)) if ev1 else None
 
+    # One model sharded over the ranks (whole tensors, plan_shards), strong scaling: device time of
+    # compress_shard + decompress_shard, max over ranks.
+    sharded = None
+    if world > 1:
+        ts = []
+        for s_i in range(3):
+            barrier()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            loc = z.compress_shard(model, rank, world, readback_to_cpu=False)
+            back = z.decompress_shard(loc)
+            b.record()
+            torch.cuda.synchronize()
+            if s_i:
+                ts.append(a.elapsed_time(b) / 1e3)
+            del loc, back
+        t_sh = max_over_ranks(sum(ts) / len(ts))
+        sharded = {"value": round(model_bytes / t_sh / GB, 3), "unit": "GB/s", "ms_per_step": round(t_sh * 1e3, 3),
+                   "scaling": "strong", "workload": "one copy of the model, whole tensors per rank (plan_shards)"}
+
     # End to end through the public API from pinned host memory: H2D of the inputs, CPU blobs,
     # H2D of the blobs, and a D2H read of a result word each step.
     host = [t.cpu().pin_memory() for t in model] if not args.no_e2e else []
@@ -423,6 +444,7 @@ def main() -> None:
             "cpu_baseline": cpu_baseline,
             "clocks": clocks.summary(),
             "e2e": e2e,
+            "sharded": sharded,
             "gpu_launches": gpu_launches,
         }
         print(json.dumps(line), flush=True)

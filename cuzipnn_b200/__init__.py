@@ -10,6 +10,7 @@ from ._codec import (
     hash_tensor_with_crc32,
     last_decode_status,
 )
+from ._shard import compress_shard, decompress_shard, gather_index, plan_shards
 
 __all__ = [
     "compress_tensor",
@@ -19,4 +20,8 @@ __all__ = [
     "decompress_tensors",
     "hash_tensor_with_crc32",
     "last_decode_status",
+    "plan_shards",
+    "compress_shard",
+    "decompress_shard",
+    "gather_index",
 ]
