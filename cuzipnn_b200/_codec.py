@@ -472,6 +472,7 @@ def _ptr_array(ctype, values):
     return (ctype * len(values))(*values)
 
 
+_PIPELINE_BYTES = 1 << 29  # sub-batch of host-resident inputs (upload overlapped with the kernels)
 _COPY_BATCH_MAX = 1 << 29  # largest single copy of one zn_copy_chunks launch (65535 tiles of 8 KiB)
 
 
@@ -533,9 +534,12 @@ def compress_tensors(
     readback_to_cpu: bool = True,
 ) -> list[torch.Tensor]:
     """compress_tensor over a list of tensors, with one kernel launch per stage for all tensors of
-    an element size (and one host synchronization in all).  Each blob equals compress_tensor's.
+    an element size.  Each blob equals compress_tensor's.
 
-    With readback_to_cpu=False the blobs are views into one shared GPU buffer."""
+    With readback_to_cpu=False the blobs are views into one shared GPU buffer per batch.  Host
+    inputs are uploaded in batches of about _PIPELINE_BYTES on a side stream, so that uploads,
+    kernels and (with readback_to_cpu) downloads of different batches overlap; with pin_memory the
+    read-back blobs of a batch are views into one pinned buffer."""
     blobs: list[torch.Tensor | None] = [None] * len(tensors)
     groups: dict[tuple[int, bool], list[int]] = {}
     small: list[int] = []  # stored path and empty tensors, handled after the coded launches
@@ -578,59 +582,108 @@ def compress_tensors(
         return blobs  # type: ignore[return-value]
     first = tensors[next(iter(groups.values()))[0]]
     device = _gpu(first.detach(), _check_device(compute_device))
+    # Host-resident inputs go up in sub-batches on a copy stream, so that the upload of one batch
+    # overlaps the kernels of the previous one (and, with readback, the download of the one before).
+    host_inputs = any(not tensors[i].is_cuda for idx in groups.values() for i in idx)
+    batches: list[tuple[int, bool, list[int]]] = []
+    for (k, reorder), idx in groups.items():
+        cur: list[int] = []
+        cur_bytes = 0
+        for i in idx:
+            nb = tensors[i].numel() * k
+            if host_inputs and cur and cur_bytes + nb > _PIPELINE_BYTES:
+                batches.append((k, reorder, cur))
+                cur, cur_bytes = [], 0
+            cur.append(i)
+            cur_bytes += nb
+        batches.append((k, reorder, cur))
     pending = []
     with torch.cuda.device(device):
-        stream = _stream(device)
-        for (k, reorder), idx in groups.items():
-            xs, heads, caps, offs = [], [], [], []
-            total_cap = 0
-            for i in idx:
-                x = tensors[i].detach()
-                x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous().view(-1)
-                if x.data_ptr() % 16:
-                    x = x.clone()
-                xs.append(x)
-                heads.append(_header(tensors[i], _FLAG_REORDER if reorder else 0, chunk_bytes, 0))
-                cap = int(_lib.lib.zn_compress_bound(x.numel(), k, tensors[i].dim(), chunk_bytes))
-                caps.append(cap)
-                offs.append(total_cap)
-                total_cap += (cap + 255) & ~255
-            out = torch.empty(total_cap, dtype=torch.uint8, device=device)
-            sizes = torch.empty(len(idx), dtype=torch.int64, device=device)
-            nj = len(idx)
-            n_arr = _ptr_array(ctypes.c_int64, [x.numel() for x in xs])
-            tb = int(_lib.lib.zn_compress_batch_temp_bytes(nj, n_arr, k, chunk_bytes, sub_chunks))
-            temp = torch.empty(max(tb, 1), dtype=torch.uint8, device=device)
-            hbufs = [ctypes.create_string_buffer(h, len(h)) for h in heads]
-            _lib.check(
-                _lib.lib.zn_compress_batch(
-                    nj, _ptr_array(ctypes.c_void_p, [x.data_ptr() for x in xs]), n_arr, k, int(reorder),
-                    _ptr_array(ctypes.c_void_p, [ctypes.addressof(h) for h in hbufs]),
-                    _ptr_array(ctypes.c_int, [len(h) for h in heads]), chunk_bytes, sub_chunks,
-                    float(passthrough_threshold),
-                    _ptr_array(ctypes.c_void_p, [out.data_ptr() + o for o in offs]),
-                    _ptr_array(ctypes.c_int64, caps), sizes.data_ptr(), temp.data_ptr(), tb, stream,
-                ),
-                "zn_compress_batch",
-            )
-            pending.append((idx, out, offs, sizes, xs, temp))
+        stream = torch.cuda.current_stream(device)
+        copy_in = torch.cuda.Stream(device) if host_inputs else stream
+        for k, reorder, idx in batches:
+            with torch.cuda.stream(copy_in):
+                xs = []
+                for i in idx:
+                    x = tensors[i].detach()
+                    x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous().view(-1)
+                    if x.data_ptr() % 16:
+                        x = x.clone()
+                    xs.append(x)
+            if copy_in is not stream:
+                stream.wait_stream(copy_in)
+                for x in xs:
+                    x.record_stream(stream)
+            out, offs, sizes, temp = _launch_compress_batch(
+                device, xs, [tensors[i] for i in idx], k, reorder, chunk_bytes, sub_chunks, passthrough_threshold)
+            sizes_host = None
+            if readback_to_cpu:  # each batch's sizes come back on their own, batches keep running
+                sizes_host = torch.empty(len(idx), dtype=torch.int64, pin_memory=True)
+                sizes_host.copy_(sizes, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(stream)
+            pending.append((idx, out, offs, sizes, sizes_host, done, xs, temp))
         # The small tensors' host work overlaps the coded kernels.
         compress_small(device)
-        all_sizes = torch.cat([p[3] for p in pending]).cpu().tolist()  # the one synchronization
-        pos = 0
-        for idx, out, offs, _, _, _ in pending:
-            for i, o in zip(idx, offs):
-                size = all_sizes[pos]
-                pos += 1
-                comp = out[o : o + size]
-                if readback_to_cpu:
-                    blob = _populated_empty(size, pin_memory=pin_memory)
-                    blob.copy_(comp, non_blocking=pin_memory)
-                    comp = blob
-                blobs[i] = comp
-        if readback_to_cpu and pin_memory:
-            torch.cuda.current_stream(device).synchronize()
+        if not readback_to_cpu:
+            all_sizes = torch.cat([p[3] for p in pending]).cpu().tolist()  # the one synchronization
+            pos = 0
+            for idx, out, offs, *_ in pending:
+                for i, o in zip(idx, offs):
+                    blobs[i] = out[o : o + all_sizes[pos]]
+                    pos += 1
+            return blobs  # type: ignore[return-value]
+        copy_out = torch.cuda.Stream(device)
+        for idx, out, offs, _, sizes_host, done, _, _ in pending:
+            done.synchronize()
+            sizes_b = sizes_host.tolist()
+            if pin_memory:  # one pinned buffer per batch (cheaper than one pinned allocation per blob)
+                hoffs = [0]
+                for size in sizes_b:
+                    hoffs.append(hoffs[-1] + ((size + 15) & ~15))
+                hbuf = torch.empty(hoffs[-1], dtype=torch.uint8, pin_memory=True)
+            copy_out.wait_event(done)
+            with torch.cuda.stream(copy_out):
+                for j, (i, o, size) in enumerate(zip(idx, offs, sizes_b)):
+                    blob = hbuf[hoffs[j] : hoffs[j] + size] if pin_memory else _populated_empty(size)
+                    blob.copy_(out[o : o + size], non_blocking=pin_memory)
+                    blobs[i] = blob
+        # Blobs are complete on return, and the device buffers outlive every copy that reads them.
+        copy_out.synchronize()
+        stream.synchronize()
     return blobs  # type: ignore[return-value]
+
+
+def _launch_compress_batch(device, xs, srcs, k, reorder, chunk_bytes, sub_chunks, threshold):
+    """zn_compress_batch for device tensors `xs` (flat, 16-byte aligned; `srcs` the original
+    tensors, for the headers) on the current stream: one blob buffer holding every blob at
+    offs[j] (capacity zn_compress_bound each) and a device int64 size per blob."""
+    heads, caps, offs = [], [], []
+    total_cap = 0
+    for x, t in zip(xs, srcs):
+        heads.append(_header(t, _FLAG_REORDER if reorder else 0, chunk_bytes, 0))
+        cap = int(_lib.lib.zn_compress_bound(x.numel(), k, t.dim(), chunk_bytes))
+        caps.append(cap)
+        offs.append(total_cap)
+        total_cap += (cap + 255) & ~255
+    out = torch.empty(total_cap, dtype=torch.uint8, device=device)
+    nj = len(xs)
+    sizes = torch.empty(nj, dtype=torch.int64, device=device)
+    n_arr = _ptr_array(ctypes.c_int64, [x.numel() for x in xs])
+    tb = int(_lib.lib.zn_compress_batch_temp_bytes(nj, n_arr, k, chunk_bytes, sub_chunks))
+    temp = torch.empty(max(tb, 1), dtype=torch.uint8, device=device)
+    hbufs = [ctypes.create_string_buffer(h, len(h)) for h in heads]
+    _lib.check(
+        _lib.lib.zn_compress_batch(
+            nj, _ptr_array(ctypes.c_void_p, [x.data_ptr() for x in xs]), n_arr, k, int(reorder),
+            _ptr_array(ctypes.c_void_p, [ctypes.addressof(h) for h in hbufs]),
+            _ptr_array(ctypes.c_int, [len(h) for h in heads]), chunk_bytes, sub_chunks, float(threshold),
+            _ptr_array(ctypes.c_void_p, [out.data_ptr() + o for o in offs]),
+            _ptr_array(ctypes.c_int64, caps), sizes.data_ptr(), temp.data_ptr(), tb, _stream(device),
+        ),
+        "zn_compress_batch",
+    )
+    return out, offs, sizes, temp
 
 
 def decompress_tensors(
@@ -714,43 +767,68 @@ def decompress_tensors(
         return outs  # type: ignore[return-value]
     first = blobs[next(iter(groups.values()))[0][0]]
     device = _gpu(first, compute_device)
+    # Host-resident blobs go up in sub-batches on a copy stream, so that the upload of one batch
+    # overlaps the decoding of the previous one.
+    host_blobs = any(not blobs[i].is_cuda for items in groups.values() for i, _ in items)
+    batches: list[tuple[int, bool, list]] = []
+    for (k, reorder), items in groups.items():
+        cur: list = []
+        cur_bytes = 0
+        for item in items:
+            nb = blobs[item[0]].numel()
+            if host_blobs and cur and cur_bytes + nb > _PIPELINE_BYTES:
+                batches.append((k, reorder, cur))
+                cur, cur_bytes = [], 0
+            cur.append(item)
+            cur_bytes += nb
+        batches.append((k, reorder, cur))
     with torch.cuda.device(device):
-        stream = _stream(device)
+        stream = torch.cuda.current_stream(device)
+        copy_in = torch.cuda.Stream(device) if host_blobs else stream
+        # One status word per coded blob of this call (last_decode_status ORs them).
+        status = torch.zeros(sum(len(b[2]) for b in batches), dtype=torch.int32, device=device)
         uploaded = []
-        for (k, reorder), items in groups.items():
-            xs, ys, meta = [], [], []
-            for i, (dtype, shape, chunk_bytes, n_comp, n) in items:
-                x = blobs[i].detach().to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
-                if x.data_ptr() % 8:
-                    x = x.clone()
-                if blobs[i].is_pinned():
+        pos = 0
+        for k, reorder, items in batches:
+            with torch.cuda.stream(copy_in):
+                xs = []
+                for i, _ in items:
+                    x = blobs[i].detach().to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+                    if x.data_ptr() % 8:
+                        x = x.clone()
+                    xs.append(x)
+                if any(blobs[i].is_pinned() for i, _ in items):
                     ev = torch.cuda.Event()
-                    ev.record()
+                    ev.record(copy_in)
                     uploaded.append(ev)
-                xs.append(x)
-                y = torch.empty(shape, dtype=dtype, device=device)
-                ys.append(y)
+            if copy_in is not stream:
+                stream.wait_stream(copy_in)
+                for x in xs:
+                    x.record_stream(stream)
+            ys, meta = [], []
+            for i, (dtype, shape, chunk_bytes, n_comp, n) in items:
+                ys.append(torch.empty(shape, dtype=dtype, device=device))
                 meta.append((n, len(shape), chunk_bytes, n_comp))
             nj = len(items)
             n_arr = _ptr_array(ctypes.c_int64, [m[0] for m in meta])
             c_arr = _ptr_array(ctypes.c_int64, [m[2] for m in meta])
             tb = int(_lib.lib.zn_decompress_batch_temp_bytes(nj, n_arr, k, c_arr))
             temp = torch.empty(max(tb, 1), dtype=torch.uint8, device=device)
-            status = torch.zeros(nj, dtype=torch.int32, device=device)
             _lib.check(
                 _lib.lib.zn_decompress_batch(
                     nj, _ptr_array(ctypes.c_void_p, [x.data_ptr() for x in xs]),
                     _ptr_array(ctypes.c_int64, [x.numel() for x in xs]), n_arr, k, int(reorder),
                     _ptr_array(ctypes.c_int, [m[1] for m in meta]), c_arr,
                     _ptr_array(ctypes.c_int64, [m[3] for m in meta]),
-                    _ptr_array(ctypes.c_void_p, [y.data_ptr() for y in ys]), status.data_ptr(),
-                    temp.data_ptr(), tb, stream,
+                    _ptr_array(ctypes.c_void_p, [y.data_ptr() for y in ys]), status.data_ptr() + 4 * pos,
+                    temp.data_ptr(), tb, stream.cuda_stream,
                 ),
                 "zn_decompress_batch",
             )
-            _LAST_STATUS[device.index] = status
+            pos += nj
             for (i, _), y in zip(items, ys):
                 outs[i] = y
+        _LAST_STATUS[device.index] = status
         decompress_small()
         for ev in uploaded:
             ev.synchronize()

@@ -70,3 +70,40 @@ def test_batch_many_tensors():
     for t, y in zip(ts, ys):
         assert torch.equal(bits(y), bits(t))
     assert torch.equal(batch[17].cpu(), z.compress_tensor(ts[17]))
+
+
+@pytest.mark.parametrize("pin", [True, False])
+def test_host_inputs_pipelined_in_sub_batches(monkeypatch, pin):
+    """Host tensors go up in several sub-batches (copy stream overlapped with the kernels); blobs
+    still equal the per-tensor ones, and host blobs decode back in sub-batches too."""
+    from cuzipnn_b200 import _codec
+
+    monkeypatch.setattr(_codec, "_PIPELINE_BYTES", 1 << 20)
+    ts = [t.cpu() for t in mixed_tensors()]
+    if pin:
+        ts = [t.pin_memory() if t.is_contiguous() else t for t in ts]
+    batch = z.compress_tensors(ts, readback_to_cpu=True, pin_memory=pin)
+    for t, b in zip(ts, batch):
+        assert not b.is_cuda
+        assert torch.equal(b, z.compress_tensor(t))
+    outs = z.decompress_tensors(batch)
+    assert z.last_decode_status() == 0
+    for t, y in zip(ts, outs):
+        assert y.is_cuda and y.dtype == t.dtype and y.shape == t.shape
+        assert torch.equal(bits(y.cpu()), bits(t))
+
+
+def test_status_covers_every_group(monkeypatch):
+    """A corrupt blob in the first element-size group is reported even when later groups decode
+    cleanly (one status word per coded blob of the call)."""
+    from cuzipnn_b200 import _codec
+
+    monkeypatch.setattr(_codec, "_PIPELINE_BYTES", 1 << 20)
+    ts = mixed_tensors()
+    blobs = [b.clone() for b in z.compress_tensors(ts, readback_to_cpu=True)]
+    bad = blobs[0]
+    bad[40:44] = torch.tensor([0xFF, 0xFF, 0xFF, 0x7F], dtype=torch.uint8)  # stored size past the end
+    z.decompress_tensors(blobs)
+    assert z.last_decode_status() != 0
+    z.decompress_tensors([b for i, b in enumerate(blobs) if i != 0])
+    assert z.last_decode_status() == 0
