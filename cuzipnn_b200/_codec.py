@@ -606,10 +606,11 @@ def compress_tensors(
                 xs = []
                 for i in idx:
                     x = tensors[i].detach()
-                    x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous().view(-1)
-                    if x.data_ptr() % 16:
-                        x = x.clone()
-                    xs.append(x)
+                    if not (x.device == device and x.is_contiguous() and x.data_ptr() % 16 == 0):
+                        x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+                        if x.data_ptr() % 16:
+                            x = x.clone()
+                    xs.append(x.view(-1))
             if copy_in is not stream:
                 stream.wait_stream(copy_in)
                 for x in xs:
@@ -730,25 +731,22 @@ def decompress_tensors(
 
     # Headers of GPU blobs come to the host in one copy per device.
     plen = [min(b.numel(), _FIXED.size + 8 * _MAX_NDIM) for b in blobs]
-    prefixes: list[torch.Tensor | None] = [None] * len(blobs)
+    prefixes: list[memoryview | None] = [None] * len(blobs)
     by_dev: dict[torch.device, list[int]] = {}
     for i, b in enumerate(blobs):
         if b.is_cuda:
             by_dev.setdefault(b.device, []).append(i)
         else:
-            prefixes[i] = b.detach()[: plen[i]].contiguous()
+            prefixes[i] = memoryview(b.detach()[: plen[i]].contiguous().numpy())
     for idx in by_dev.values():
-        flat = torch.cat([blobs[i].detach()[: plen[i]] for i in idx]).cpu()
+        flat = memoryview(torch.cat([blobs[i].detach()[: plen[i]] for i in idx]).cpu().numpy())
         pos = 0
         for i in idx:
             prefixes[i] = flat[pos : pos + plen[i]]
             pos += plen[i]
     for i, blob in enumerate(blobs):
         blob = blob.detach()
-        pre = prefixes[i]
-        dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(
-            (ctypes.c_byte * plen[i]).from_address(pre.data_ptr())
-        )
+        dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefixes[i])
         if flags & _FLAG_STORED or n == 0:
             small.append((i, dtype, shape, flags))
             continue
@@ -793,9 +791,11 @@ def decompress_tensors(
             with torch.cuda.stream(copy_in):
                 xs = []
                 for i, _ in items:
-                    x = blobs[i].detach().to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
-                    if x.data_ptr() % 8:
-                        x = x.clone()
+                    x = blobs[i].detach()
+                    if not (x.device == device and x.is_contiguous() and x.data_ptr() % 8 == 0):
+                        x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+                        if x.data_ptr() % 8:
+                            x = x.clone()
                     xs.append(x)
                 if any(blobs[i].is_pinned() for i, _ in items):
                     ev = torch.cuda.Event()

@@ -283,6 +283,27 @@ __device__ __forceinline__ void load_raw_round(const uint8_t* const* src, const 
   }
 }
 
+// 16 elements (4 * K little-endian words) from their K byte planes (4 words each), with the
+// exponent reorder undone.  bf16 has a direct form: with E the exponent plane (high bytes after
+// the reorder, e8) and B the sign / mantissa plane (s m7), the element's high byte is
+// s | e8 >> 1 and its low byte (e8 & 1) << 7 | m7, four elements per 32-bit operation.
+template <int K, bool REORDER>
+__device__ __forceinline__ void assemble_elements(const uint32_t (*p)[4], uint32_t* e) {
+  if constexpr (K == 2 && REORDER) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t E = p[1][i], B = p[0][i];
+      const uint32_t hi = (B & 0x80808080u) | ((E >> 1) & 0x7F7F7F7Fu);
+      const uint32_t lo = ((E << 7) & 0x80808080u) | (B & 0x7F7F7F7Fu);
+      e[2 * i] = __byte_perm(lo, hi, 0x5140);
+      e[2 * i + 1] = __byte_perm(lo, hi, 0x7362);
+    }
+  } else {
+    planes_to_elements<K>(p, e);
+    reorder_words<K, REORDER, false>(e, 4 * K);
+  }
+}
+
 // KC: coded planes per chunk held in shared memory.  The main pass (KC = 1 for K > 1) flags
 // chunks with more coded planes; a second pass with KC = K decodes only those.
 // Work split: a warp item is 8 sub-chunks; lane l of 8-lane segment g runs chain c on sub-chunk
@@ -429,7 +450,71 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
       }
     uint32_t pn[kChains][K][4];
     load_raw_round<K, kChains>(src, coded, base, len, 0, l, pn);
-    for (int r = 0; r < rounds; ++r) {
+    int r = 0;
+    if constexpr (KC == 1 && kChains == 1) {
+      // Full rounds (all 16 steps of this lane's state valid): no per-step predication, 32-bit
+      // bookkeeping and running raw / output pointers; the partial rounds at the end of a
+      // sub-chunk take the general loop below.
+      const int64_t l16 = int64_t(l) * kSteps;
+      const int rfull = len[0] >= l16 + kSteps ? int((len[0] - l16 - kSteps) / kRound) + 1 : 0;
+      Cursor& cb = cur[0][0];
+      uint4* ring = const_cast<uint4*>(reinterpret_cast<const uint4*>(ring16[0][0]));
+      const uint32_t end8 = (cb.end + 7) & ~7u;
+      const uint8_t* rp[K];
+#pragma unroll
+      for (int b = 0; b < K; ++b) rp[b] = src[b] + base[0] + l16;
+      uint8_t* op = outc + (base[0] + l16) * K;  // 16-byte aligned when outc is (full rounds)
+      for (; r < rfull; ++r) {
+        if (ncoded > 0) {
+          const uint32_t need = min((cb.ptr + 16 + 7) & ~7u, end8);
+          while (cb.fill < need) {
+            ring[(cb.fill / 8) & (RH / 8 - 1)] = load_block(gb[0], cb.fill / 8, lo[0], hi[0]);
+            cb.fill += 8;
+          }
+          const uint32_t limit = min((cb.ptr + RH) & ~7u, end8);
+          cb.nload = limit > cb.fill ? min((limit - cb.fill) / 8, 2u) : 0u;
+          if (cb.nload > 0) cb.r0 = load_block(gb[0], cb.fill / 8, lo[0], hi[0]);
+          if (cb.nload > 1) cb.r1 = load_block(gb[0], cb.fill / 8 + 1, lo[0], hi[0]);
+        }
+        uint32_t p[K][4];
+#pragma unroll
+        for (int b = 0; b < K; ++b)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) p[b][i] = pn[0][b][i];
+        if (r + 1 < rfull) {
+#pragma unroll
+          for (int b = 0; b < K; ++b) {
+            if (coded[b]) continue;
+            const uint2* sp = reinterpret_cast<const uint2*>(rp[b] + kRound);
+            const uint2 v0 = sp[0], v1 = sp[1];
+            pn[0][b][0] = v0.x; pn[0][b][1] = v0.y; pn[0][b][2] = v1.x; pn[0][b][3] = v1.y;
+          }
+        } else if (r + 1 < rounds) {
+          load_raw_round<K, kChains>(src, coded, base, len, r + 1, l, pn);
+        }
+        if (ncoded > 0) {
+          int nact[1] = {kSteps};
+          uint32_t acc[1][4] = {};
+          decode_round<true, RH>(cur[0], tabs, ring16[0], nact, acc);
+#pragma unroll
+          for (int b = 0; b < K; ++b)
+            if (b == pslot[0]) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) p[b][i] = acc[0][i];
+            }
+          if (cb.nload > 0) ring[(cb.fill / 8) & (RH / 8 - 1)] = cb.r0;
+          if (cb.nload > 1) ring[(cb.fill / 8 + 1) & (RH / 8 - 1)] = cb.r1;
+          cb.fill += 8 * cb.nload;
+        }
+        uint32_t e[4 * K];
+        assemble_elements<K, REORDER>(p, e);
+        store_words(op, e, 4 * K, out16);
+#pragma unroll
+        for (int b = 0; b < K; ++b) rp[b] += kRound;
+        op += kRound * K;
+      }
+    }
+    for (; r < rounds; ++r) {
       int nact[kChains];
       int64_t off[kChains];
 #pragma unroll
@@ -500,8 +585,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
       for (int c = 0; c < kChains; ++c) {
         if (nact[c] <= 0) continue;
         uint32_t e[4 * K];
-        planes_to_elements<K>(p[c], e);
-        reorder_words<K, REORDER, false>(e, 4 * K);
+        assemble_elements<K, REORDER>(p[c], e);
         uint8_t* dst = outc + (base[c] + off[c]) * K;
         if (nact[c] == 16) {
           store_words(dst, e, 4 * K, out16 && ((((base[c] + off[c]) * K) & 15) == 0));
