@@ -151,20 +151,46 @@ __device__ __forceinline__ uint64_t reorder_elem(uint64_t u) {
 
 // The 16 symbols of plane b for elements e0 .. e0 + 15 of a chunk (nact of them valid).
 // mode: 2 = 16-byte loads, 1 = 8-byte loads, 0 = bytes.
+// Byte plane b (after the exponent reorder) of 16 elements given as 4 * K little-endian words.
+// bf16 has a direct form: the exponent byte of element u is (u >> 7) & 0xFF and the sign /
+// mantissa byte (u >> 8 & 0x80) | (u & 0x7F), two elements per word.
 template <int K, bool REORDER>
-__device__ __forceinline__ void plane_symbols(const uint8_t* xc, int64_t e0, int nact, int b, int mode, uint32_t* sym) {
-  if (nact == 16 && mode) {
-    uint32_t e[4 * K];
-    load_words(xc + e0 * K, e, 4 * K, mode == 2);
-    reorder_words<K, REORDER, true>(e, 4 * K);
+__device__ __forceinline__ void plane_of_elements(const uint32_t* e, int b, uint32_t* sym) {
+  if constexpr (K == 2 && REORDER) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t t0 = e[2 * i], t1 = e[2 * i + 1];
+      if (b == 1) {
+        t0 >>= 7;
+        t1 >>= 7;
+      } else {
+        t0 = (t0 & 0x007F007Fu) | ((t0 >> 8) & 0x00800080u);
+        t1 = (t1 & 0x007F007Fu) | ((t1 >> 8) & 0x00800080u);
+      }
+      sym[i] = __byte_perm(t0, t1, 0x6420);
+    }
+  } else {
+    uint32_t w[4 * K];
+#pragma unroll
+    for (int i = 0; i < 4 * K; ++i) w[i] = e[i];
+    reorder_words<K, REORDER, true>(w, 4 * K);
     uint32_t p[K][4];
-    elements_to_planes<K>(e, p);
+    elements_to_planes<K>(w, p);
 #pragma unroll
     for (int q = 0; q < K; ++q)
       if (q == b) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) sym[i] = p[q][i];
       }
+  }
+}
+
+template <int K, bool REORDER>
+__device__ __forceinline__ void plane_symbols(const uint8_t* xc, int64_t e0, int nact, int b, int mode, uint32_t* sym) {
+  if (nact == 16 && mode) {
+    uint32_t e[4 * K];
+    load_words(xc + e0 * K, e, 4 * K, mode == 2);
+    plane_of_elements<K, REORDER>(e, b, sym);
     return;
   }
   uint64_t lo = 0, hi = 0;  // two 64-bit accumulators keep the runtime-indexed bytes in registers
@@ -186,11 +212,25 @@ constexpr int kHistDepth = 4;
 
 template <int K, bool REORDER, int VB>
 __device__ __forceinline__ void hist_count(uint32_t (&w)[VB / 4], uint32_t* hist, int col) {
-  reorder_words<K, REORDER, true>(w, VB / 4);
+  if constexpr (K == 2 && REORDER) {
+    // bf16 (two elements per word): exponent bytes (u >> 7) & 0xFF at bytes 0 and 2 of w >> 7,
+    // sign / mantissa bytes (u >> 8 & 0x80) | (u & 0x7F) at bytes 0 and 2 of v.
 #pragma unroll
-  for (int q = 0; q < VB; ++q) {
-    const uint32_t byte = (w[q >> 2] >> (8 * (q & 3))) & 0xFF;
-    atomicAdd(&hist[(((q % K) << 8) | byte) * kCols + col], 1u);
+    for (int q = 0; q < VB / 4; ++q) {
+      const uint32_t t = w[q] >> 7;
+      const uint32_t v = (w[q] & 0x007F007Fu) | ((w[q] >> 8) & 0x00800080u);
+      atomicAdd(&hist[(v & 0xFF) * kCols + col], 1u);
+      atomicAdd(&hist[(256 + (t & 0xFF)) * kCols + col], 1u);
+      atomicAdd(&hist[((v >> 16) & 0xFF) * kCols + col], 1u);
+      atomicAdd(&hist[(256 + ((t >> 16) & 0xFF)) * kCols + col], 1u);
+    }
+  } else {
+    reorder_words<K, REORDER, true>(w, VB / 4);
+#pragma unroll
+    for (int q = 0; q < VB; ++q) {
+      const uint32_t byte = (w[q >> 2] >> (8 * (q & 3))) & 0xFF;
+      atomicAdd(&hist[(((q % K) << 8) | byte) * kCols + col], 1u);
+    }
   }
 }
 
@@ -279,8 +319,8 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const EncArgs* __res
 template <bool FULL, int I>
 __device__ __forceinline__ void encode_step(uint32_t& x, uint32_t& wp, uint16_t* stage, const uint32_t* sym,
                                             const uint4* tab, bool act) {
-  const uint4 e = tab[get_byte(sym, I)];  // {magic, bias, (M - f) | shift << 16, f}
-  const bool emit = (FULL || act) && (x >> 20) >= e.w;
+  const uint4 e = tab[get_byte(sym, I)];  // {magic, bias, (M - f) | shift << 16, f * 2^20 - 1}
+  const bool emit = (FULL || act) && x > e.w;
   wp -= emit;
   if (emit) stage[wp & 31] = uint16_t(x);
   x = emit ? x >> 16 : x;
@@ -435,11 +475,11 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const EncArgs* __re
       const uint32_t f = ff[h];
       uint4 e = make_uint4(0, 0, 0, 0);
       if (f == 1) {
-        e = make_uint4(0xFFFFFFFFu, cum + kM - 1, (kM - 1) | (0u << 16), 1u);
+        e = make_uint4(0xFFFFFFFFu, cum + kM - 1, (kM - 1) | (0u << 16), (1u << 20) - 1u);
       } else if (f > 1) {
         const int l = 32 - __clz(f - 1);
         const uint32_t mg = uint32_t(((uint64_t((uint64_t(1) << l) - f) << 32) / f) + 1);
-        e = make_uint4(mg, cum, (kM - f) | (uint32_t(l - 1) << 16), f);
+        e = make_uint4(mg, cum, (kM - f) | (uint32_t(l - 1) << 16), uint32_t((uint64_t(f) << 20) - 1));
       }
       etab[b * 256 + s] = e;
       cum += f;
@@ -528,15 +568,7 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const EncArgs* __re
         const int64_t off = int64_t(r) * kRound + l * kSteps;
         nact[c] = int(max(int64_t(0), min(int64_t(kSteps), len[c] - off)));
         if (full_round(c, r)) {
-          reorder_words<K, REORDER, true>(nxt[c], 4 * K);
-          uint32_t pl[K][4];
-          elements_to_planes<K>(nxt[c], pl);
-#pragma unroll
-          for (int q = 0; q < K; ++q)
-            if (q == b) {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) sym[c][i] = pl[q][i];
-            }
+          plane_of_elements<K, REORDER>(nxt[c], b, sym[c]);
         } else {
           plane_symbols<K, REORDER>(xc, base[c] + off, nact[c], b, 0, sym[c]);
         }
