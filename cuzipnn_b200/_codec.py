@@ -473,6 +473,7 @@ def _ptr_array(ctype, values):
 
 
 _PIPELINE_BYTES = 1 << 29  # sub-batch of host-resident inputs (upload overlapped with the kernels)
+_DEVICE_BATCH_BYTES = 1 << 31  # sub-batch of device-resident inputs (launched while the host prepares the next)
 _COPY_BATCH_MAX = 1 << 29  # largest single copy of one zn_copy_chunks launch (65535 tiles of 8 KiB)
 
 
@@ -533,8 +534,9 @@ def compress_tensors(
     compute_device: torch.device | str | None = None,
     readback_to_cpu: bool = True,
 ) -> list[torch.Tensor]:
-    """compress_tensor over a list of tensors, with one kernel launch per stage for all tensors of
-    an element size.  Each blob equals compress_tensor's.
+    """compress_tensor over a list of tensors, with one kernel launch per stage for each batch of
+    tensors of an element size (batches of about _DEVICE_BATCH_BYTES, launched while the host
+    prepares the next).  Each blob equals compress_tensor's.
 
     With readback_to_cpu=False the blobs are views into one shared GPU buffer per batch.  Host
     inputs are uploaded in batches of about _PIPELINE_BYTES on a side stream, so that uploads,
@@ -591,7 +593,7 @@ def compress_tensors(
         cur_bytes = 0
         for i in idx:
             nb = tensors[i].numel() * k
-            if host_inputs and cur and cur_bytes + nb > _PIPELINE_BYTES:
+            if cur and cur_bytes + nb > (_PIPELINE_BYTES if host_inputs else _DEVICE_BATCH_BYTES):
                 batches.append((k, reorder, cur))
                 cur, cur_bytes = [], 0
             cur.append(i)
@@ -693,11 +695,12 @@ def decompress_tensors(
     compute_device: torch.device | str | None = None,
     readback_to_cpu: bool = False,
 ) -> list[torch.Tensor]:
-    """decompress_tensor over a list of blobs, with one kernel launch per stage for all blobs of an
-    element size.  Decoding errors are reported by last_decode_status()."""
+    """decompress_tensor over a list of blobs, with one kernel launch per stage for each batch of
+    blobs of an element size (batches of about _DEVICE_BATCH_BYTES, or _PIPELINE_BYTES for host
+    blobs, launched while the host prepares the next).  Decoding errors are reported by
+    last_decode_status()."""
     compute_device = _check_device(compute_device)
     outs: list[torch.Tensor | None] = [None] * len(blobs)
-    groups: dict[tuple[int, bool], list[tuple[int, tuple]]] = {}
     for blob in blobs:
         if blob.dtype != torch.uint8 or blob.dim() != 1:
             raise ValueError("blob must be a 1-D uint8 tensor")
@@ -738,12 +741,66 @@ def decompress_tensors(
             by_dev.setdefault(b.device, []).append(i)
         else:
             prefixes[i] = memoryview(b.detach()[: plen[i]].contiguous().numpy())
-    for idx in by_dev.values():
-        flat = memoryview(torch.cat([blobs[i].detach()[: plen[i]] for i in idx]).cpu().numpy())
-        pos = 0
-        for i in idx:
-            prefixes[i] = flat[pos : pos + plen[i]]
-            pos += plen[i]
+    for dev, idx in by_dev.items():
+        for i, view in zip(idx, _gather_prefixes(dev, [blobs[i].detach() for i in idx], [plen[i] for i in idx])):
+            prefixes[i] = view
+
+    # Coded blobs are launched in batches as they are parsed, so that the GPU starts on the first
+    # batch while the host prepares the next.  Host-resident blobs go up on a copy stream in
+    # smaller batches, so that the upload of one batch overlaps the decoding of the previous one.
+    device: torch.device | None = None
+    stream = copy_in = status = None
+    uploaded: list[torch.cuda.Event] = []
+    pos = 0
+    cur: dict[tuple[int, bool], tuple[list, int]] = {}
+
+    def launch(k: int, reorder: bool, items: list) -> None:
+        nonlocal copy_in, pos
+        host = any(not blobs[i].is_cuda for i, _ in items)
+        if host and copy_in is None:
+            copy_in = torch.cuda.Stream(device)
+        up = copy_in if host else stream
+        with torch.cuda.stream(up):
+            xs = []
+            for i, _ in items:
+                x = blobs[i].detach()
+                if not (x.device == device and x.is_contiguous() and x.data_ptr() % 8 == 0):
+                    x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+                    if x.data_ptr() % 8:
+                        x = x.clone()
+                xs.append(x)
+            if any(blobs[i].is_pinned() for i, _ in items):
+                ev = torch.cuda.Event()
+                ev.record(up)
+                uploaded.append(ev)
+        if up is not stream:
+            stream.wait_stream(up)
+            for x in xs:
+                x.record_stream(stream)
+        ys, meta = [], []
+        for i, (dtype, shape, chunk_bytes, n_comp, n) in items:
+            ys.append(torch.empty(shape, dtype=dtype, device=device))
+            meta.append((n, len(shape), chunk_bytes, n_comp))
+        nj = len(items)
+        n_arr = _ptr_array(ctypes.c_int64, [m[0] for m in meta])
+        c_arr = _ptr_array(ctypes.c_int64, [m[2] for m in meta])
+        tb = int(_lib.lib.zn_decompress_batch_temp_bytes(nj, n_arr, k, c_arr))
+        temp = torch.empty(max(tb, 1), dtype=torch.uint8, device=device)
+        _lib.check(
+            _lib.lib.zn_decompress_batch(
+                nj, _ptr_array(ctypes.c_void_p, [x.data_ptr() for x in xs]),
+                _ptr_array(ctypes.c_int64, [x.numel() for x in xs]), n_arr, k, int(reorder),
+                _ptr_array(ctypes.c_int, [m[1] for m in meta]), c_arr,
+                _ptr_array(ctypes.c_int64, [m[3] for m in meta]),
+                _ptr_array(ctypes.c_void_p, [y.data_ptr() for y in ys]), status.data_ptr() + 4 * pos,
+                temp.data_ptr(), tb, stream.cuda_stream,
+            ),
+            "zn_decompress_batch",
+        )
+        pos += nj
+        for (i, _), y in zip(items, ys):
+            outs[i] = y
+
     for i, blob in enumerate(blobs):
         blob = blob.detach()
         dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefixes[i])
@@ -757,77 +814,27 @@ def decompress_tensors(
         _, _, data_off = _layout(len(shape), k * nch, n_comp)
         if blob.numel() < data_off:
             raise ValueError("blob is truncated")
-        groups.setdefault((k, bool(flags & _FLAG_REORDER)), []).append(
-            (i, (dtype, shape, chunk_bytes, n_comp, n))
-        )
-    if not groups:
+        if device is None:
+            device = _gpu(blob, compute_device)
+            stream = torch.cuda.current_stream(device)
+            # One status word per coded blob of this call (last_decode_status ORs them).
+            status = torch.zeros(len(blobs), dtype=torch.int32, device=device)
+        key = (k, bool(flags & _FLAG_REORDER))
+        items, nbytes = cur.get(key, ([], 0))
+        items.append((i, (dtype, shape, chunk_bytes, n_comp, n)))
+        nbytes += blob.numel()
+        if nbytes >= (_PIPELINE_BYTES if not blob.is_cuda else _DEVICE_BATCH_BYTES):
+            with torch.cuda.device(device):
+                launch(key[0], key[1], items)
+            items, nbytes = [], 0
+        cur[key] = (items, nbytes)
+    if device is None:
         decompress_small()
         return outs  # type: ignore[return-value]
-    first = blobs[next(iter(groups.values()))[0][0]]
-    device = _gpu(first, compute_device)
-    # Host-resident blobs go up in sub-batches on a copy stream, so that the upload of one batch
-    # overlaps the decoding of the previous one.
-    host_blobs = any(not blobs[i].is_cuda for items in groups.values() for i, _ in items)
-    batches: list[tuple[int, bool, list]] = []
-    for (k, reorder), items in groups.items():
-        cur: list = []
-        cur_bytes = 0
-        for item in items:
-            nb = blobs[item[0]].numel()
-            if host_blobs and cur and cur_bytes + nb > _PIPELINE_BYTES:
-                batches.append((k, reorder, cur))
-                cur, cur_bytes = [], 0
-            cur.append(item)
-            cur_bytes += nb
-        batches.append((k, reorder, cur))
     with torch.cuda.device(device):
-        stream = torch.cuda.current_stream(device)
-        copy_in = torch.cuda.Stream(device) if host_blobs else stream
-        # One status word per coded blob of this call (last_decode_status ORs them).
-        status = torch.zeros(sum(len(b[2]) for b in batches), dtype=torch.int32, device=device)
-        uploaded = []
-        pos = 0
-        for k, reorder, items in batches:
-            with torch.cuda.stream(copy_in):
-                xs = []
-                for i, _ in items:
-                    x = blobs[i].detach()
-                    if not (x.device == device and x.is_contiguous() and x.data_ptr() % 8 == 0):
-                        x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
-                        if x.data_ptr() % 8:
-                            x = x.clone()
-                    xs.append(x)
-                if any(blobs[i].is_pinned() for i, _ in items):
-                    ev = torch.cuda.Event()
-                    ev.record(copy_in)
-                    uploaded.append(ev)
-            if copy_in is not stream:
-                stream.wait_stream(copy_in)
-                for x in xs:
-                    x.record_stream(stream)
-            ys, meta = [], []
-            for i, (dtype, shape, chunk_bytes, n_comp, n) in items:
-                ys.append(torch.empty(shape, dtype=dtype, device=device))
-                meta.append((n, len(shape), chunk_bytes, n_comp))
-            nj = len(items)
-            n_arr = _ptr_array(ctypes.c_int64, [m[0] for m in meta])
-            c_arr = _ptr_array(ctypes.c_int64, [m[2] for m in meta])
-            tb = int(_lib.lib.zn_decompress_batch_temp_bytes(nj, n_arr, k, c_arr))
-            temp = torch.empty(max(tb, 1), dtype=torch.uint8, device=device)
-            _lib.check(
-                _lib.lib.zn_decompress_batch(
-                    nj, _ptr_array(ctypes.c_void_p, [x.data_ptr() for x in xs]),
-                    _ptr_array(ctypes.c_int64, [x.numel() for x in xs]), n_arr, k, int(reorder),
-                    _ptr_array(ctypes.c_int, [m[1] for m in meta]), c_arr,
-                    _ptr_array(ctypes.c_int64, [m[3] for m in meta]),
-                    _ptr_array(ctypes.c_void_p, [y.data_ptr() for y in ys]), status.data_ptr() + 4 * pos,
-                    temp.data_ptr(), tb, stream.cuda_stream,
-                ),
-                "zn_decompress_batch",
-            )
-            pos += nj
-            for (i, _), y in zip(items, ys):
-                outs[i] = y
+        for (k, reorder), (items, _) in cur.items():
+            if items:
+                launch(k, reorder, items)
         _LAST_STATUS[device.index] = status
         decompress_small()
         for ev in uploaded:
@@ -839,6 +846,24 @@ def decompress_tensors(
                     host.copy_(y)
                     outs[i] = host
     return outs  # type: ignore[return-value]
+
+
+def _gather_prefixes(device: torch.device, bs: list[torch.Tensor], plen: list[int]) -> list[memoryview]:
+    """The first plen[j] bytes of each device blob, in one device-to-host copy: a batched device
+    copy into one buffer when every blob is 8-byte aligned, else a concatenation."""
+    with torch.cuda.device(device):
+        step = _FIXED.size + 8 * _MAX_NDIM
+        if all(b.data_ptr() % 8 == 0 for b in bs) and all(p > 0 for p in plen):
+            buf = torch.empty(len(bs) * step, dtype=torch.uint8, device=device)
+            _copy_batch(device, [b.data_ptr() for b in bs], [buf.data_ptr() + j * step for j in range(len(bs))], plen)
+            flat = memoryview(buf.cpu().numpy())
+            return [flat[j * step : j * step + p] for j, p in enumerate(plen)]
+        flat = memoryview(torch.cat([b[:p] for b, p in zip(bs, plen)]).cpu().numpy())
+        out, pos = [], 0
+        for p in plen:
+            out.append(flat[pos : pos + p])
+            pos += p
+        return out
 
 
 def _populated_empty(size: int, *, pin_memory: bool = False) -> torch.Tensor:

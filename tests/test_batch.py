@@ -107,3 +107,19 @@ def test_status_covers_every_group(monkeypatch):
     assert z.last_decode_status() != 0
     z.decompress_tensors([b for i, b in enumerate(blobs) if i != 0])
     assert z.last_decode_status() == 0
+
+
+def test_device_inputs_in_sub_batches(monkeypatch):
+    """Device tensors in several launch batches (the GPU starts on one while the host prepares the
+    next): blobs equal the per-tensor ones and decode back exactly."""
+    from cuzipnn_b200 import _codec
+
+    monkeypatch.setattr(_codec, "_DEVICE_BATCH_BYTES", 1 << 20)
+    ts = mixed_tensors()
+    batch = z.compress_tensors(ts, readback_to_cpu=False)
+    for t, b in zip(ts, batch):
+        assert torch.equal(b.cpu(), z.compress_tensor(t))
+    outs = z.decompress_tensors(batch)
+    assert z.last_decode_status() == 0
+    for t, y in zip(ts, outs):
+        assert torch.equal(bits(y.cpu()), bits(t.cpu()))
