@@ -757,19 +757,11 @@ __device__ __forceinline__ void warp_copy16(uint8_t* __restrict__ dst, const uin
     reinterpret_cast<uint16_t*>(dst + t0)[lane] = reinterpret_cast<const uint16_t*>(src + t0)[lane];
 }
 
-// Exclusive prefix sums of the nu * 8 stream lengths of a payload into pre[] (shared), by all
-// kPackThreads threads (two lengths per thread, up to 512).
-__device__ void stream_prefix(const uint8_t* meta, int64_t tb, const Geom& g, int32_t* pre, int32_t* warp_tot) {
-  const int S = g.nu * kLanes, t = threadIdx.x, lane = t & 31, w = t >> 5;
-  int32_t v[2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int fi = 2 * t + h;
-    v[h] = fi >= S ? 0
-           : g.lw == 2 ? int32_t(reinterpret_cast<const uint16_t*>(meta + tb)[fi])
-                       : int32_t(reinterpret_cast<const uint32_t*>(meta + tb)[fi]);
-  }
-  int32_t incl = v[0] + v[1];
+// Exclusive prefix sums of two values per thread (kPackThreads threads) into out[2 t], out[2 t + 1];
+// out[2 * kPackThreads] gets the total.  Ends with a barrier.
+__device__ void block_scan_pairs(int32_t v0, int32_t v1, int32_t* out, int32_t* warp_tot) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  int32_t incl = v0 + v1;
   for (int o = 1; o < 32; o <<= 1) {
     const int32_t x = __shfl_up_sync(0xFFFFFFFFu, incl, o);
     if (lane >= o) incl += x;
@@ -779,57 +771,112 @@ __device__ void stream_prefix(const uint8_t* meta, int64_t tb, const Geom& g, in
   __syncthreads();
   int32_t base = 0;
   for (int q = 0; q < w; ++q) base += warp_tot[q];
-  const int32_t ex = base + incl - v[0] - v[1];
-  pre[2 * t] = ex;
-  pre[2 * t + 1] = ex + v[0];
+  const int32_t ex = base + incl - v0 - v1;
+  out[2 * t] = ex;
+  out[2 * t + 1] = ex + v0;
+  if (t == kPackThreads - 1) out[2 * kPackThreads] = ex + v0 + v1;
   __syncthreads();
 }
 
-// Copy part `part` of `nparts` of one coded payload to dst (8-byte aligned): the meta block (part
-// 0), then its share of the nu * 8 streams, each from the tail of its scratch slot to its place
-// after the meta block (from the prefix sums of the stream lengths).  One warp per item.  Called
-// by all threads of the CTA.
-__device__ void copy_payload(const EncArgs& a, uint64_t u, int64_t m, uint8_t* dst, int npres, int part, int nparts,
-                             int32_t* pre, int32_t* warp_tot) {
+// Shared-memory staging of the payload copy: 16-byte blocks, filled by cp.async.
+constexpr int kStageBlocks = 1024;  // 16 KiB
+
+struct PayloadSmem {
+  int32_t pre[2 * kPackThreads + 1];   // stream start, halfwords after the meta block
+  int32_t bpre[2 * kPackThreads + 1];  // first staged block of each stream
+  int32_t warp_tot[kPackThreads / 32];
+  uint4 stage[kStageBlocks];
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = uint32_t(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+
+// Copy one coded payload to dst (8-byte aligned): the meta block, then the nu * 8 streams, each
+// from the tail of its scratch slot to its place after the meta block.  The 16-byte blocks that
+// hold a window of streams are first fetched into shared memory with cp.async (all in flight at
+// once, one wait), then each warp writes its streams out of shared memory, shifted into place.
+// A stream longer than the window is copied straight from global memory.  Called by all
+// kPackThreads threads of the CTA.
+__device__ void copy_payload(const EncArgs& a, uint64_t u, int64_t m, uint8_t* dst, int npres, PayloadSmem& P) {
   const uint8_t* meta = a.meta + u * a.meta_slot;
   const Geom g = geom_of(m, a.t);
   const int64_t tb = table_bytes(npres);
   const int64_t mh = meta_bytes(npres, g) / 2;
-  stream_prefix(meta, tb, g, pre, warp_tot);
-  const int S = g.nu * kLanes;
-  const int f0 = int(int64_t(S) * part / nparts), f1 = int(int64_t(S) * (part + 1) / nparts);
-  const int lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int S = g.nu * kLanes, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = kPackThreads / 32;
+  if (warp == nwarps - 1) warp_copy16(dst, meta, 2 * mh, lane);
   const uint16_t* streams = a.streams + u * a.unit_words;
-  for (int it = f0 - (part == 0) + int(threadIdx.x >> 5); it < f1; it += nwarps) {
-    if (it < f0) {  // the meta block (table, lengths, states)
-      warp_copy16(dst, meta, 2 * mh, lane);
-      continue;
-    }
-    const int32_t n = it + 1 < S ? pre[it + 1] - pre[it]
-                      : (g.lw == 2 ? int32_t(reinterpret_cast<const uint16_t*>(meta + tb)[it])
-                                   : int32_t(reinterpret_cast<const uint32_t*>(meta + tb)[it]));
-    const int gi = it / kLanes, l = it % kLanes;
-    const uint16_t* src = streams + int64_t(gi) * a.sub_words + int64_t(l) * a.lane_words + (a.lane_words - n);
-    warp_copy16(dst + 2 * (mh + int64_t(pre[it])), reinterpret_cast<const uint8_t*>(src), 2 * int64_t(n), lane);
+  auto src_of = [&](int fi, int32_t n) {
+    return reinterpret_cast<const uint8_t*>(streams + int64_t(fi / kLanes) * a.sub_words +
+                                            int64_t(fi % kLanes) * a.lane_words + (a.lane_words - n));
+  };
+  auto len_of = [&](int fi) {
+    return fi >= S ? 0 : g.lw == 2 ? int32_t(reinterpret_cast<const uint16_t*>(meta + tb)[fi])
+                                   : int32_t(reinterpret_cast<const uint32_t*>(meta + tb)[fi]);
+  };
+  int32_t n2[2], nb2[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int fi = 2 * tid + h;
+    n2[h] = len_of(fi);
+    const uintptr_t s0 = n2[h] ? reinterpret_cast<uintptr_t>(src_of(fi, n2[h])) : 0;
+    nb2[h] = n2[h] ? int32_t(((s0 + 2 * uint32_t(n2[h]) + 15) >> 4) - (s0 >> 4)) : 0;
   }
-  __syncthreads();
+  block_scan_pairs(n2[0], n2[1], P.pre, P.warp_tot);
+  block_scan_pairs(nb2[0], nb2[1], P.bpre, P.warp_tot);
+  for (int fa = 0; fa < S;) {
+    // The window: streams [fa, fb) whose blocks fit in the staging buffer (at least stream fa).
+    int fb = fa + 1;
+    for (int st = 256; st > 0; st >>= 1)
+      if (fb + st <= S && P.bpre[fb + st] - P.bpre[fa] <= kStageBlocks) fb += st;
+    const int32_t b0 = P.bpre[fa], nb = P.bpre[fb] - b0;
+    if (nb > kStageBlocks) {  // one stream longer than the window: straight from global memory
+      const int32_t n = P.pre[fa + 1] - P.pre[fa];
+      if (warp == 0) warp_copy16(dst + 2 * (mh + int64_t(P.pre[fa])), src_of(fa, n), 2 * int64_t(n), lane);
+    } else {
+      int span = 1;
+      while (span < fb - fa) span <<= 1;
+      for (int32_t jb = tid; jb < nb; jb += kPackThreads) {
+        int fi = fa;  // stream of staged block jb: largest fi in [fa, fb) with bpre[fi] <= b0 + jb
+        for (int st = span >> 1; st > 0; st >>= 1)
+          if (fi + st < fb && P.bpre[fi + st] <= b0 + jb) fi += st;
+        const int32_t n = P.pre[fi + 1] - P.pre[fi];
+        const uint8_t* s0 = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(src_of(fi, n)) & ~uintptr_t(15));
+        cp_async16(&P.stage[jb], s0 + 16 * int64_t(b0 + jb - P.bpre[fi]));
+      }
+      asm volatile("cp.async.commit_group;\n" ::: "memory");
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+      __syncthreads();
+      for (int fi = fa + warp; fi < fb; fi += nwarps) {
+        const int32_t n = P.pre[fi + 1] - P.pre[fi];
+        if (!n) continue;
+        const uintptr_t off = reinterpret_cast<uintptr_t>(src_of(fi, n)) & 15;
+        warp_copy16(dst + 2 * (mh + int64_t(P.pre[fi])),
+                    reinterpret_cast<const uint8_t*>(&P.stage[P.bpre[fi] - b0]) + off, 2 * int64_t(n), lane);
+      }
+    }
+    __syncthreads();
+    fa = fb;
+  }
 }
 
-// Grid (chunk, part): part p of chunk j handles 1/kPackParts of every coded payload and of the
-// chunk's elements for the raw planes.  Chunks run in reverse order, so the most recently encoded
-// (and read) chunks are still in L2.
-constexpr int kPackParts = 8;
+// One CTA per (chunk, part), the parts of a chunk adjacent in launch order: part p of chunk j
+// splits out 1/kPackParts of the chunk's elements for the raw planes, and part 0 also copies the
+// chunk's coded payloads.  Chunks run in reverse order, so the most recently encoded (and read)
+// chunks are still in L2.
+constexpr int kPackParts = 4;
 template <int K>
 constexpr int kPackGroups = K >= 4 ? 1 : 4 / K;
 
 template <int K, bool REORDER>
 __global__ void __launch_bounds__(kPackThreads, 4) pack_kernel(const EncArgs* __restrict__ jobs, int njobs, int64_t total_chunks) {
-  __shared__ int32_t pre[512];
-  __shared__ int32_t warp_tot[kPackThreads / 32];
-  const int64_t gj = total_chunks - 1 - blockIdx.x;
+  __shared__ PayloadSmem P;
+  const int64_t gj = total_chunks - 1 - blockIdx.x / kPackParts;
   const EncArgs& a = jobs[find_job(jobs, njobs, gj)];
   const int64_t j = gj - a.chunk0;
-  const int part = blockIdx.y;
+  const int part = int(blockIdx.x % kPackParts);
   const int64_t m = min(a.C, a.n - j * a.C);
   const int64_t data_off = a.scalars[0];
   __shared__ int npres[K];
@@ -873,7 +920,7 @@ __global__ void __launch_bounds__(kPackThreads, 4) pack_kernel(const EncArgs* __
       if (!coded[b]) continue;
       const uint64_t u = uint64_t(b) * a.nch + j;
       const int64_t size = a.comp_bytes[u];
-      copy_payload(a, u, m, dst[b], npres[b], 0, 1, pre, warp_tot);
+      copy_payload(a, u, m, dst[b], npres[b], P);
       if (threadIdx.x < 8 && size + threadIdx.x < align8(size)) dst[b][size + threadIdx.x] = 0;
     }
   }
@@ -932,11 +979,10 @@ __global__ void __launch_bounds__(kPackThreads) assemble_kernel(const EncArgs* _
     return;
   }
   __shared__ int npres;
-  __shared__ int32_t pre[512];
-  __shared__ int32_t warp_tot[kPackThreads / 32];
+  __shared__ PayloadSmem P;
   if (threadIdx.x == 0) npres = count_present(a.meta + uint64_t(i) * a.meta_slot);
   __syncthreads();
-  copy_payload(a, uint64_t(i), in_bytes[i], reinterpret_cast<uint8_t*>(out_ptrs[i]), npres, 0, 1, pre, warp_tot);
+  copy_payload(a, uint64_t(i), in_bytes[i], reinterpret_cast<uint8_t*>(out_ptrs[i]), npres, P);
   if (threadIdx.x == 0) { out_bytes[i] = size; statuses[i] = 0; }
 }
 
@@ -1019,7 +1065,7 @@ template <int K, bool REORDER>
 void launch_pack(const EncArgs* jobs, int njobs, int64_t grid, cudaStream_t s) {
   if (grid <= 0) return;
   TimedLaunch tl("pack", s);
-  pack_kernel<K, REORDER><<<dim3(unsigned(grid), kPackParts), kPackThreads, 0, s>>>(jobs, njobs, grid);
+  pack_kernel<K, REORDER><<<unsigned(grid * kPackParts), kPackThreads, 0, s>>>(jobs, njobs, grid);
   count_launch();
 }
 
@@ -1142,7 +1188,7 @@ int zn_compress_batch(int njobs, const void* const* x, const int64_t* n, int k, 
     memcpy(a.header, headers[i], size_t(hb));
     chunk0 += a.nch;
   }
-  if (chunk0 > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_compress: too many chunks");
+  if (chunk0 > 0x7FFFFFFF / kPackParts) return set_error(ZN_ERR_INVALID, "zn_compress: too many chunks");
   EncArgs* dj = reinterpret_cast<EncArgs*>(tb);
   if (int rc = upload_jobs(jobs.data(), njobs, dj, chunk0, s)) return rc;
   int rc = ZN_OK;
