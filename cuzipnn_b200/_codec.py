@@ -474,6 +474,7 @@ def _ptr_array(ctype, values):
 
 _PIPELINE_BYTES = 1 << 29  # sub-batch of host-resident inputs (upload overlapped with the kernels)
 _DEVICE_BATCH_BYTES = 1 << 31  # sub-batch of device-resident inputs (launched while the host prepares the next)
+_TINY_BYTES = 65536  # stored tensors up to this size decode into views of one shared buffer per call
 _COPY_BATCH_MAX = 1 << 29  # largest single copy of one zn_copy_chunks launch (65535 tiles of 8 KiB)
 
 
@@ -503,19 +504,21 @@ def _stored_blobs_gpu(items: list[tuple[int, torch.Tensor, bytes]], device: torc
     heads = b"".join(h for _, _, h in items)
     hdev = torch.frombuffer(bytearray(heads), dtype=torch.uint8).pin_memory().to(device, non_blocking=True)
     srcs, dsts, sizes = [], [], []
-    hpos = 0
+    hpos, hbase, obase = 0, hdev.data_ptr(), out.data_ptr()
     for (_, x, head), o in zip(items, offs):
-        srcs.append(hdev.data_ptr() + hpos)
-        dsts.append(out.data_ptr() + o)
-        sizes.append(len(head))
-        hpos += len(head)
+        hl = len(head)
+        srcs.append(hbase + hpos)
+        dsts.append(obase + o)
+        sizes.append(hl)
+        hpos += hl
         nb = x.numel() * x.element_size()
         if nb:
-            x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
-            if x.data_ptr() % 8:
-                x = x.clone()
+            if not (x.device == device and x.is_contiguous() and x.data_ptr() % 8 == 0):
+                x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+                if x.data_ptr() % 8:
+                    x = x.clone()
             srcs.append(x.data_ptr())
-            dsts.append(out.data_ptr() + o + len(head))
+            dsts.append(obase + o + hl)
             sizes.append(nb)
     # `hdev` and the staged inputs were allocated on this stream, so the caching allocator reuses
     # their memory only after the copy has run.
@@ -547,8 +550,13 @@ def compress_tensors(
     small: list[int] = []  # stored path and empty tensors, handled after the coded launches
     sub_chunks = _sub_chunks(chunk_bytes, sub_chunk_bytes) if sub_chunk_bytes > 0 else 0
     for i, t in enumerate(tensors):
-        dev, sub_chunks = _check_args(t, chunk_bytes, sub_chunk_bytes, passthrough_threshold, min_compress_bytes,
-                                      None, pin_memory, compute_device, readback_to_cpu)
+        if i == 0:  # the scalar arguments once, then each tensor's dtype and rank
+            _, sub_chunks = _check_args(t, chunk_bytes, sub_chunk_bytes, passthrough_threshold, min_compress_bytes,
+                                        None, pin_memory, compute_device, readback_to_cpu)
+        elif t.dtype not in _CODES:
+            raise TypeError(f"unsupported dtype {t.dtype}")
+        elif t.dim() > _MAX_NDIM:
+            raise ValueError(f"at most {_MAX_NDIM} dimensions are supported")
         k, n = t.element_size(), t.numel()
         if n * k < min_compress_bytes or n == 0:
             small.append(i)
@@ -557,11 +565,12 @@ def compress_tensors(
 
     def compress_small(device: torch.device | None) -> None:
         batch = []
+        cd = _check_device(compute_device)
         for i in small:
             t = tensors[i]
             k, n = t.element_size(), t.numel()
             if (device is not None and not readback_to_cpu and n * k <= _COPY_BATCH_MAX
-                    and _gpu(t.detach(), _check_device(compute_device)) == device):
+                    and (t.device == device if cd is None and t.is_cuda else _gpu(t, cd) == device)):
                 stored = n * k < min_compress_bytes
                 flags = _FLAG_STORED if stored else _FLAG_REORDER if t.dtype in _REORDER else 0
                 batch.append((i, t.detach(), _header(t, flags, 0 if stored else chunk_bytes, 0)))
@@ -698,7 +707,8 @@ def decompress_tensors(
     """decompress_tensor over a list of blobs, with one kernel launch per stage for each batch of
     blobs of an element size (batches of about _DEVICE_BATCH_BYTES, or _PIPELINE_BYTES for host
     blobs, launched while the host prepares the next).  Decoding errors are reported by
-    last_decode_status()."""
+    last_decode_status().  Stored-path tensors of up to _TINY_BYTES decoded on the GPU are views
+    into one buffer per call (one allocation instead of one per small tensor)."""
     compute_device = _check_device(compute_device)
     outs: list[torch.Tensor | None] = [None] * len(blobs)
     for blob in blobs:
@@ -709,26 +719,39 @@ def decompress_tensors(
     def decompress_small() -> None:
         """Stored blobs on the GPU decode into GPU tensors by one batched copy; the rest (CPU blobs,
         CPU outputs, empty tensors) take decompress_tensor."""
-        srcs, dsts, sizes = [], [], []
+        srcs, dsts, sizes, tiny = [], [], [], []
         bdev = None  # the one device whose stored blobs are batched
         for i, dtype, shape, flags in small:
-            b = blobs[i].detach()
+            b = blobs[i]
             header_size = _FIXED.size + 8 * len(shape)
             nbytes = math.prod(shape) * dtype.itemsize
             if (flags & _FLAG_STORED and b.is_cuda and not readback_to_cpu and 0 < nbytes <= _COPY_BATCH_MAX
-                    and (b.data_ptr() + header_size) % 8 == 0 and _gpu(b, compute_device) == b.device
+                    and (b.data_ptr() + header_size) % 8 == 0
+                    and (compute_device is None or _gpu(b, compute_device) == b.device)
                     and bdev in (None, b.device)):
                 bdev = b.device
                 if b.numel() < header_size + nbytes:
                     raise ValueError("blob is truncated")
-                y = torch.empty(shape, dtype=dtype, device=b.device)
                 srcs.append(b.data_ptr() + header_size)
-                dsts.append(y.data_ptr())
                 sizes.append(nbytes)
-                outs[i] = y
+                if nbytes <= _TINY_BYTES:  # placed in one shared buffer below
+                    tiny.append((i, dtype, shape, nbytes, len(dsts)))
+                    dsts.append(0)
+                else:
+                    y = torch.empty(shape, dtype=dtype, device=b.device)
+                    dsts.append(y.data_ptr())
+                    outs[i] = y
             else:
                 outs[i] = decompress_tensor(b, compute_device=compute_device, readback_to_cpu=readback_to_cpu)
         if srcs:
+            if tiny:
+                total = sum((nb + 255) & ~255 for _, _, _, nb, _ in tiny)
+                buf = torch.empty(total, dtype=torch.uint8, device=bdev)
+                pos = 0
+                for i, dtype, shape, nb, j in tiny:
+                    outs[i] = buf[pos : pos + nb].view(dtype).view(shape)
+                    dsts[j] = buf.data_ptr() + pos
+                    pos += (nb + 255) & ~255
             with torch.cuda.device(bdev):
                 _copy_batch(bdev, srcs, dsts, sizes)
 
@@ -740,9 +763,9 @@ def decompress_tensors(
         if b.is_cuda:
             by_dev.setdefault(b.device, []).append(i)
         else:
-            prefixes[i] = memoryview(b.detach()[: plen[i]].contiguous().numpy())
+            prefixes[i] = memoryview(b[: plen[i]].contiguous().numpy())
     for dev, idx in by_dev.items():
-        for i, view in zip(idx, _gather_prefixes(dev, [blobs[i].detach() for i in idx], [plen[i] for i in idx])):
+        for i, view in zip(idx, _gather_prefixes(dev, [blobs[i] for i in idx], [plen[i] for i in idx])):
             prefixes[i] = view
 
     # Coded blobs are launched in batches as they are parsed, so that the GPU starts on the first
@@ -763,7 +786,7 @@ def decompress_tensors(
         with torch.cuda.stream(up):
             xs = []
             for i, _ in items:
-                x = blobs[i].detach()
+                x = blobs[i]
                 if not (x.device == device and x.is_contiguous() and x.data_ptr() % 8 == 0):
                     x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
                     if x.data_ptr() % 8:
@@ -802,7 +825,6 @@ def decompress_tensors(
             outs[i] = y
 
     for i, blob in enumerate(blobs):
-        blob = blob.detach()
         dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefixes[i])
         if flags & _FLAG_STORED or n == 0:
             small.append((i, dtype, shape, flags))
