@@ -478,6 +478,18 @@ _TINY_BYTES = 65536  # stored tensors up to this size decode into views of one s
 _COPY_BATCH_MAX = 1 << 29  # largest single copy of one zn_copy_chunks launch (65535 tiles of 8 KiB)
 
 
+_SIDE_STREAMS: dict[tuple[int, int], torch.cuda.Stream] = {}
+
+
+def _side_stream(device: torch.device, which: int) -> torch.cuda.Stream:
+    """The upload (0) or download (1) stream of a device, created once: the caching allocator keeps
+    a pool per stream, so reusing the streams lets later calls reuse the staging memory."""
+    key = (device.index, which)
+    if key not in _SIDE_STREAMS:
+        _SIDE_STREAMS[key] = torch.cuda.Stream(device)
+    return _SIDE_STREAMS[key]
+
+
 def _copy_batch(device: torch.device, srcs: list[int], dsts: list[int], sizes: list[int]) -> None:
     """Many small device copies (8-byte aligned addresses) in one zn_copy_chunks launch; the address
     table goes to the GPU in one pinned copy."""
@@ -611,7 +623,7 @@ def compress_tensors(
     pending = []
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device)
-        copy_in = torch.cuda.Stream(device) if host_inputs else stream
+        copy_in = _side_stream(device, 0) if host_inputs else stream
         for k, reorder, idx in batches:
             with torch.cuda.stream(copy_in):
                 xs = []
@@ -634,7 +646,10 @@ def compress_tensors(
                 sizes_host.copy_(sizes, non_blocking=True)
             done = torch.cuda.Event()
             done.record(stream)
-            pending.append((idx, out, offs, sizes, sizes_host, done, xs, temp))
+            # The staged inputs and the scratch are only used on `stream` from here on, so the
+            # caching allocator may hand their memory to later batches in stream order.
+            del xs, temp
+            pending.append([idx, out, offs, sizes, sizes_host, done])
         # The small tensors' host work overlaps the coded kernels.
         compress_small(device)
         if not readback_to_cpu:
@@ -645,8 +660,9 @@ def compress_tensors(
                     blobs[i] = out[o : o + all_sizes[pos]]
                     pos += 1
             return blobs  # type: ignore[return-value]
-        copy_out = torch.cuda.Stream(device)
-        for idx, out, offs, _, sizes_host, done, _, _ in pending:
+        copy_out = _side_stream(device, 1)
+        for entry in pending:
+            idx, out, offs, _, sizes_host, done = entry
             done.synchronize()
             sizes_b = sizes_host.tolist()
             if pin_memory:  # one pinned buffer per batch (cheaper than one pinned allocation per blob)
@@ -660,6 +676,8 @@ def compress_tensors(
                     blob = hbuf[hoffs[j] : hoffs[j] + size] if pin_memory else _populated_empty(size)
                     blob.copy_(out[o : o + size], non_blocking=pin_memory)
                     blobs[i] = blob
+            out.record_stream(copy_out)  # its memory returns to the allocator after the downloads
+            entry[1] = out = None
         # Blobs are complete on return, and the device buffers outlive every copy that reads them.
         copy_out.synchronize()
         stream.synchronize()
@@ -781,7 +799,7 @@ def decompress_tensors(
         nonlocal copy_in, pos
         host = any(not blobs[i].is_cuda for i, _ in items)
         if host and copy_in is None:
-            copy_in = torch.cuda.Stream(device)
+            copy_in = _side_stream(device, 0)
         up = copy_in if host else stream
         with torch.cuda.stream(up):
             xs = []
