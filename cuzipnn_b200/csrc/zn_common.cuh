@@ -19,7 +19,7 @@ namespace zn {
 
 constexpr uint32_t kScaleBits = 12;
 constexpr uint32_t kM = 1u << kScaleBits;
-constexpr uint32_t kL = 1u << 16;
+constexpr uint32_t kL = 1u << 15;  // rANS states live in [kL, 2^31)
 constexpr int kLanes = 8;        // states per sub-chunk
 constexpr int kSteps = 16;       // symbols per lane per round
 constexpr int kRound = kLanes * kSteps;

@@ -445,7 +445,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
           cb.ptr = h0;
           cb.end = h0 + mine;
           cb.fill = h0 & ~7u;
-          err |= cb.x < kL;
+          err |= cb.x < kL || cb.x >= 0x80000000u;
         }
       }
     uint32_t pn[kChains][K][4];

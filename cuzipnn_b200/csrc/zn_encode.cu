@@ -313,20 +313,21 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const EncArgs* __res
 }
 
 // One encode step of one state for symbol byte I (last symbol first; the decoder runs forward).
-// A state that would leave [L, 2^32) after coding emits its low 16 bits into its own stream,
-// which grows down from the end of the state's slot; the word goes to the lane's 32-halfword
-// staging ring in shared memory (one predicated 2-byte store, no branch).
+// A state at or above f * 2^19 (it would leave [L, 2^31) after coding) emits its low 16 bits into
+// its own stream, which grows down from the end of the state's slot; the word goes to the lane's
+// 32-halfword staging ring in shared memory (one predicated 2-byte store, no branch).  Then
+// x' = x + bias + q * (M - f) with q = floor(x / f) = umulhi(x, magic) >> shift, exact because
+// x < 2^31; the shift sits in the low 5 bits of e.z, which the wrapping funnel shift uses.
 template <bool FULL, int I>
 __device__ __forceinline__ void encode_step(uint32_t& x, uint32_t& wp, uint16_t* stage, const uint32_t* sym,
                                             const uint4* tab, bool act) {
-  const uint4 e = tab[get_byte(sym, I)];  // {magic, bias, (M - f) | shift << 16, f * 2^20 - 1}
+  const uint4 e = tab[get_byte(sym, I)];  // {magic, bias, (M - f) << 5 | shift, f * 2^19 - 1}
   const bool emit = (FULL || act) && x > e.w;
   wp -= emit;
   if (emit) stage[wp & 31] = uint16_t(x);
   x = emit ? x >> 16 : x;
-  const uint32_t tq = __umulhi(x, e.x);
-  const uint32_t q = (tq + ((x - tq) >> 1)) >> (e.z >> 16);
-  const uint32_t xn = x + e.y + q * (e.z & 0xFFFFu);
+  const uint32_t q = __funnelshift_r(__umulhi(x, e.x), 0u, e.z);
+  const uint32_t xn = x + e.y + q * (e.z >> 5);
   x = (FULL || act) ? xn : x;
 }
 
@@ -443,18 +444,26 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const EncArgs* __re
     }
     uint32_t cum = block_excl_scan(fsum, S.red_u);
     uint32_t rank = block_excl_scan(psum, S.red_u);
-    // Entropy lower bound of the payload; skip planes that cannot beat the passthrough budget.
+    // A lower bound of the payload size; planes that cannot beat the passthrough budget are not
+    // coded (the blob is the same: such a unit is stored raw).  Per state, with y = log2(x) plus
+    // 16 per emitted word: y starts at log2(L) = 15 and ends below 32 + 16 W (W words), and a
+    // symbol of frequency f adds at least 12 - log2(f) - d bits, where the rounding of x / f costs
+    // d <= -log2(1 - f / 2^15) without an emission (x >= 2^15) and, with one, the truncation and
+    // the rounding (x >= 8 f) cost at most 2 * -log2(7 / 8) = 0.386 bits.  With I the sum of
+    // 12 - log2(f) - d over the plane's symbols and S states: 16 W + 32 > (I + 15.772) / 1.024125
+    // per state, so payload > meta + ((I + 15.772 S) / 1.024125 - 32 S) / 8 bytes.  64 bytes
+    // cover the float rounding of the sums.
     float bits = 0.f;
 #pragma unroll
     for (int h = 0; h < kEncSym; ++h)
       if (cc[h]) {
         const float fr = float(ff[h]);
-        bits += float(cc[h]) * (float(kScaleBits) - log2f(fr) + log2f(1.f - fr * (1.f / 65536.f)));
+        bits += float(cc[h]) * (float(kScaleBits) - log2f(fr) + log2f(1.f - fr * (1.f / 32768.f)));
       }
     const float info = block_sum_f(bits, S.red_f);
     const int64_t mb = meta_bytes(int(np), g);
     const float states = float(g.nu) * kLanes;
-    const float lb = 2.f * (info - 16.f * states) / 16.1f + float(mb) - 64.f - float(m) * (1.f / 1024.f);
+    const float lb = ((info + 15.772f * states) / 1.024125f - 32.f * states) * 0.125f + float(mb) - 64.f;
     const bool skip = lb >= float(thr);
     if (tid == 0) {
       S.skip[b] = skip;
@@ -465,8 +474,12 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const EncArgs* __re
       __syncthreads();
       continue;
     }
-    // Encoder table: x' = x + bias + q * (M - f), q = floor(x / f) by multiply-high
-    // (Granlund and Montgomery, "Division by invariant integers using multiplication", 1994).
+    // Encoder table: x' = x + bias + q * (M - f), q = floor(x / f) = umulhi(x, magic) >> shift
+    // (division by multiplication: Granlund and Montgomery, "Division by invariant integers using
+    // multiplication", 1994).  With shift = floor(log2 f) and magic = ceil(2^(32 + shift) / f) <
+    // 2^32 (f not a power of two) the quotient is exact for x < 2^31, since x times the magic's
+    // excess (< f <= 2^(shift + 1)) stays below 2^(32 + shift).  Powers of two use magic 2^31 and
+    // shift log2(f) - 1; f = 1 uses magic 2^32 - 1 (q = x - 1) with the bias raised by M - 1.
     for (int i = tid; i < 96; i += kEncThreads) S.fbuf[i] = 0;
     __syncthreads();
 #pragma unroll
@@ -475,11 +488,12 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const EncArgs* __re
       const uint32_t f = ff[h];
       uint4 e = make_uint4(0, 0, 0, 0);
       if (f == 1) {
-        e = make_uint4(0xFFFFFFFFu, cum + kM - 1, (kM - 1) | (0u << 16), (1u << 20) - 1u);
+        e = make_uint4(0xFFFFFFFFu, cum + kM - 1, (kM - 1) << 5, (1u << 19) - 1u);
       } else if (f > 1) {
-        const int l = 32 - __clz(f - 1);
-        const uint32_t mg = uint32_t(((uint64_t((uint64_t(1) << l) - f) << 32) / f) + 1);
-        e = make_uint4(mg, cum, (kM - f) | (uint32_t(l - 1) << 16), uint32_t((uint64_t(f) << 20) - 1));
+        const uint32_t sh = 31 - __clz(f);  // floor(log2 f)
+        const bool pow2 = (f & (f - 1)) == 0;
+        const uint32_t mg = pow2 ? 0x80000000u : uint32_t(((uint64_t(1) << (32 + sh)) + f - 1) / f);
+        e = make_uint4(mg, cum, ((kM - f) << 5) | (pow2 ? sh - 1 : sh), (f << 19) - 1u);
       }
       etab[b * 256 + s] = e;
       cum += f;

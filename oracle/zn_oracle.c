@@ -15,7 +15,7 @@
 
 #define ANS_SCALE 12
 #define ANS_M (1u << ANS_SCALE)
-#define ANS_L (1u << 16)
+#define ANS_L (1u << 15)
 #define LANES 8
 #define STEPS 16
 #define ROUND (LANES * STEPS)
@@ -240,7 +240,7 @@ int64_t orc_ans_encode(const uint8_t *sym, int64_t m, int n_sub, uint8_t *out, i
                     int64_t p = r * ROUND + l * STEPS + i;
                     if (p >= len) continue;
                     int s = sym[base + p];
-                    if ((x[l] >> 20) >= f[s]) { /* x >= f * 2^20 = ((L >> 12) << 16) * f */
+                    if ((x[l] >> 19) >= f[s]) { /* x >= f * 2^19 = ((L >> 12) << 16) * f */
                         tmp[l * per + nw[l]++] = (uint16_t)(x[l] & 0xFFFF);
                         x[l] >>= 16;
                     }
@@ -308,7 +308,7 @@ int orc_ans_decode(const uint8_t *pl, int64_t size, int64_t m, uint8_t *out) {
             spos += 2 * nw[l];
             ptr[l] = 0;
             x[l] = get32(states + 4 * fi);
-            if (x[l] < ANS_L) return -7;
+            if (x[l] < ANS_L || x[l] >= 0x80000000u) return -7;
         }
         int64_t base = (int64_t)gi * g.sc;
         int64_t len = m - base < g.sc ? m - base : g.sc;

@@ -21,7 +21,10 @@
  * (J. Duda, "Asymmetric numeral systems", 2013; F. Giesen, "Interleaved entropy coders", 2014),
  * and this file is the normative statement of that format:
  *
- *   Scale: 12 bits (M = 4096).  State: u32 in [L, 2^32) with L = 2^16.  I/O: 16-bit words.
+ *   Scale: 12 bits (M = 4096).  State: u32 in [L, 2^31) with L = 2^15.  I/O: 16-bit words.
+ *   Coding symbol s (frequency f, cumulative frequency cum) maps x to
+ *   (x / f) * M + x % f + cum; before that, a state with x >= f * 2^19 writes its low 16 bits
+ *   to its stream and shifts right by 16.  The encoder starts every state at L.
  *   A plane chunk of m symbols (1 <= m <= 2^24) is cut into sub-chunks of
  *   sc = roundup(ceil(m / n_sub), 128) symbols; nu = ceil(m / sc) of them are non-empty.
  *   Each sub-chunk is coded by 8 interleaved states ("lanes"), each with its own word stream.
