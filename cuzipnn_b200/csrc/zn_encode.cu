@@ -14,6 +14,7 @@
 //   3. pack_kernel: one CTA per chunk re-reads the chunk (in reverse order, so the most recently
 //      encoded chunks are still in L2), writes raw planes straight from the elements and copies
 //      the coded payloads from scratch, zero-padding every unit to 8 bytes.
+#include <climits>
 #include <math.h>
 #include <string.h>
 
@@ -57,6 +58,10 @@ struct EncArgs {
   uint8_t* out;             // blob buffer
   uint64_t* size_out;       // device u64 receiving the blob size
   int64_t sizes_off, idx_off;
+  // Raw planes written in place by the encoder: the blob offset a raw unit (b, j) has when every
+  // chunk codes exactly one plane and all earlier planes are raw (spec_data_off + b *
+  // spec_plane_bytes + j * align8(C)); scan checks the guess (scalars[2]) and pack skips them.
+  int64_t spec_data_off, spec_plane_bytes;
   int header_len;
   uint8_t header[24 + 8 * 64];
 };
@@ -346,7 +351,7 @@ __device__ __forceinline__ void encode_round(uint32_t* x, uint32_t* wp, uint16_t
 // ---- the encoder ----------------------------------------------------------------------------
 
 template <int K, bool REORDER>
-__global__ void __launch_bounds__(kEncThreads) encode_kernel(const EncArgs* __restrict__ jobs, int njobs) {
+__global__ void __launch_bounds__(kEncThreads, 7) encode_kernel(const EncArgs* __restrict__ jobs, int njobs) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint4* etab = reinterpret_cast<uint4*>(smem_raw);                         // [K][256]
   EncSmem& S = *reinterpret_cast<EncSmem*>(smem_raw + K * 256 * 16);
@@ -533,9 +538,19 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const EncArgs* __re
   // Phase C: encode.  A warp item is (plane, group of 8 sub-chunks); lane l of 8-lane segment g
   // runs chain c on sub-chunk 8 * group + 4 * c + g, each chain one state with its own stream slot.
   const int ngroups = int(cdiv(g.nu, 4 * kEncChains));
-  int nplanes = 0;
-  for (int b = 0; b < K; ++b) nplanes += !S.skip[b];
-  if (tid < K) S.nwsum[tid] = 0;
+  int nplanes = 0, first_coded = K;
+  uint32_t spec_mask = 0;  // skipped planes this CTA writes into the blob at their guessed offset
+  for (int b = 0; b < K; ++b) {
+    nplanes += !S.skip[b];
+    if (!S.skip[b] && first_coded == K) first_coded = b;
+  }
+  if (a.allow_skip && a.out && nplanes > 0)
+    for (int b = 0; b < K; ++b)
+      if (S.skip[b]) spec_mask |= 1u << b;
+  if (tid < K) {
+    S.nwsum[tid] = 0;
+    if ((spec_mask >> tid) & 1) a.comp_bytes[uint64_t(tid) * a.nch + j] = -2;
+  }
   __syncthreads();
   const int seg = lane >> 3, l = lane & 7;
   const int rounds = int(g.sc / kRound);
@@ -555,6 +570,8 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const EncArgs* __re
     uint16_t* stage[kEncChains];
     uint32_t x[kEncChains], wp[kEncChains], flushed[kEncChains];
     uint32_t nxt[kEncChains][4 * K];
+    uint8_t* spec0[kEncChains];  // this lane's bytes of plane 0 at the guessed blob place
+    const bool spec_item = b == first_coded && spec_mask;
 #pragma unroll
     for (int c = 0; c < kEncChains; ++c) {
       gi[c] = 4 * kEncChains * (item % ngroups) + 4 * c + seg;
@@ -565,6 +582,7 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const EncArgs* __re
       x[c] = kL;
       wp[c] = flushed[c] = uint32_t(a.lane_words);  // the stream grows down from the slot's end
       stage[c] = reinterpret_cast<uint16_t*>(S.stage[tid]);  // one ring per lane: kEncChains == 1
+      spec0[c] = spec_item ? a.out + a.spec_data_off + j * align8(a.C) + base[c] + l * kSteps : nullptr;
     }
     // The elements of the next (lower) round are loaded while the current round is encoded.
     auto full_round = [&](int c, int r) {
@@ -585,6 +603,23 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const EncArgs* __re
           plane_of_elements<K, REORDER>(nxt[c], b, sym[c]);
         } else {
           plane_symbols<K, REORDER>(xc, base[c] + off, nact[c], b, 0, sym[c]);
+        }
+        // The skipped (raw) planes of the same elements go to their guessed place in the blob.
+        if (spec_item) {
+#pragma unroll
+          for (int q = 0; q < K; ++q) {
+            if (!((spec_mask >> q) & 1)) continue;
+            uint8_t* d = spec0[c] + q * a.spec_plane_bytes + int64_t(r) * kRound;
+            uint32_t raw[4];
+            if (full_round(c, r)) {
+              plane_of_elements<K, REORDER>(nxt[c], q, raw);
+              reinterpret_cast<uint2*>(d)[0] = make_uint2(raw[0], raw[1]);
+              reinterpret_cast<uint2*>(d)[1] = make_uint2(raw[2], raw[3]);
+            } else {
+              plane_symbols<K, REORDER>(xc, base[c] + off, nact[c], q, 0, raw);
+              for (int i = 0; i < nact[c]; ++i) d[i] = uint8_t(raw[i >> 2] >> (8 * (i & 3)));
+            }
+          }
         }
         if (r > 0 && full_round(c, r - 1))
           load_words(xc + (base[c] + int64_t(r - 1) * kRound + l * kSteps) * K, nxt[c], 4 * K, mode == 2);
@@ -664,10 +699,17 @@ __device__ __forceinline__ void block_scan2(int64_t& a, int64_t& b, int64_t& ta,
 // One CTA per job.
 __global__ void __launch_bounds__(kScanThreads) scan_kernel(const EncArgs* __restrict__ jobs) {
   __shared__ int64_t sm[128];
+  __shared__ long long spec_lo, spec_hi;  // range of (guessed - final relative) offsets
   const EncArgs& a = jobs[blockIdx.x];
   const int tid = threadIdx.x;
   const int64_t last = a.n - (a.nch - 1) * a.C;
   int64_t carry_data = 0, carry_comp = 0;
+  long long dlo = LLONG_MAX, dhi = LLONG_MIN;
+  if (tid == 0) {
+    spec_lo = LLONG_MAX;
+    spec_hi = LLONG_MIN;
+  }
+  __syncthreads();
   for (int64_t start = 0; start < a.units; start += int64_t(kScanThreads) * kScanPer) {
     int64_t stored[kScanPer];
     bool use[kScanPer];
@@ -696,6 +738,12 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const EncArgs* __res
       const int64_t i = start + int64_t(tid) * kScanPer + q;
       if (i < a.units) {
         a.dst_rel[i] = (carry_data + sd) | (int64_t(use[q]) << 62);
+        if (a.comp_bytes[i] == -2) {  // written in place by the encoder: its guessed offset
+          const int64_t gb = a.spec_data_off + (i / a.nch) * a.spec_plane_bytes + (i % a.nch) * align8(a.C);
+          const long long d = gb - (carry_data + sd);
+          dlo = d < dlo ? d : dlo;
+          dhi = d > dhi ? d : dhi;
+        }
         if (use[q]) *reinterpret_cast<int32_t*>(a.out + a.idx_off + 4 * (carry_comp + sc)) = int32_t(i);
         sd += align8(stored[q]);
         sc += use[q];
@@ -707,6 +755,10 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const EncArgs* __res
   const int64_t n_comp = carry_comp;
   const int64_t data_off = align8(a.idx_off + 4 * n_comp);
   const int64_t size = data_off + carry_data;
+  // The in-place raw units are usable only if every one of them landed where the blob has it.
+  atomicMin(&spec_lo, dlo);
+  atomicMax(&spec_hi, dhi);
+  __syncthreads();
   for (int i = tid; i < a.header_len; i += kScanThreads) {
     uint8_t v = a.header[i];
     if (i >= 12 && i < 16) v = uint8_t(uint64_t(n_comp) >> (8 * (i - 12)));
@@ -716,6 +768,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const EncArgs* __res
   if (tid == 0) {
     a.scalars[0] = data_off;
     a.scalars[1] = size;
+    a.scalars[2] = spec_lo == LLONG_MAX || (spec_lo == data_off && spec_hi == data_off);
     *a.size_out = uint64_t(size);
   }
 }
@@ -895,8 +948,9 @@ __global__ void __launch_bounds__(kPackThreads, 4) pack_kernel(const EncArgs* __
   const int64_t data_off = a.scalars[0];
   __shared__ int npres[K];
   uint8_t* dst[K];
-  bool coded[K];
+  bool coded[K], raw_w[K];  // raw_w: a raw plane this kernel writes (not already in place)
   bool any_raw = false, any_coded = false;
+  const bool spec_ok = a.scalars[2] != 0;
   if (part == 0 && threadIdx.x < K) {
     const uint64_t u = uint64_t(threadIdx.x) * a.nch + j;
     npres[threadIdx.x] = (a.dst_rel[u] >> 62) & 1 ? count_present(a.meta + u * a.meta_slot) : 0;
@@ -907,7 +961,8 @@ __global__ void __launch_bounds__(kPackThreads, 4) pack_kernel(const EncArgs* __
     const int64_t d = a.dst_rel[u];
     coded[b] = (d >> 62) & 1;
     dst[b] = a.out + data_off + (d & ((int64_t(1) << 62) - 1));
-    any_raw |= !coded[b];
+    raw_w[b] = !coded[b] && !(spec_ok && a.comp_bytes[u] == -2);
+    any_raw |= raw_w[b];
     any_coded |= coded[b];
   }
   // Raw planes: this part's 16-element groups, kPackGroups per thread per pass (128 input bytes).
@@ -938,8 +993,7 @@ __global__ void __launch_bounds__(kPackThreads, 4) pack_kernel(const EncArgs* __
       if (threadIdx.x < 8 && size + threadIdx.x < align8(size)) dst[b][size + threadIdx.x] = 0;
     }
   }
-  if (!any_raw) return;
-  for (; vb < g1; vb += G * kPackThreads) {
+  for (; any_raw && vb < g1; vb += G * kPackThreads) {
     if (vb != g0 + threadIdx.x) {
 #pragma unroll
       for (int d = 0; d < G; ++d) {
@@ -956,7 +1010,7 @@ __global__ void __launch_bounds__(kPackThreads, 4) pack_kernel(const EncArgs* __
       elements_to_planes<K>(e[d], p);
 #pragma unroll
       for (int b = 0; b < K; ++b)
-        if (!coded[b]) {
+        if (raw_w[b]) {
           uint8_t* q = dst[b] + v * 16;
           if ((reinterpret_cast<uintptr_t>(q) & 15) == 0) *reinterpret_cast<uint4*>(q) = make_uint4(p[b][0], p[b][1], p[b][2], p[b][3]);
           else {
@@ -967,11 +1021,11 @@ __global__ void __launch_bounds__(kPackThreads, 4) pack_kernel(const EncArgs* __
     }
   }
   if (part != kPackParts - 1) return;
-  for (int64_t e1 = (mode ? m / 16 : 0) * 16 + threadIdx.x; e1 < m; e1 += kPackThreads) {
+  for (int64_t e1 = (mode ? m / 16 : 0) * 16 + threadIdx.x; any_raw && e1 < m; e1 += kPackThreads) {
     const uint64_t w = reorder_elem<K, REORDER>(load_elem<K>(xc + e1 * K));
 #pragma unroll
     for (int b = 0; b < K; ++b)
-      if (!coded[b]) dst[b][e1] = uint8_t(w >> (8 * b));
+      if (raw_w[b]) dst[b][e1] = uint8_t(w >> (8 * b));
   }
   if (threadIdx.x < 8 && m + threadIdx.x < align8(m)) {
 #pragma unroll
@@ -1198,6 +1252,8 @@ int zn_compress_batch(int njobs, const void* const* x, const int64_t* n, int k, 
     a.size_out = sizes_out + i;
     a.sizes_off = hb;
     a.idx_off = hb + 4 * a.units;
+    a.spec_data_off = align8(a.idx_off + 4 * a.nch);
+    a.spec_plane_bytes = a.nch ? (a.nch - 1) * align8(chunk_bytes) + align8(n[i] - (a.nch - 1) * chunk_bytes) : 0;
     a.header_len = hb;
     memcpy(a.header, headers[i], size_t(hb));
     chunk0 += a.nch;

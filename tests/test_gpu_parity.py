@@ -220,3 +220,22 @@ def test_corrupt_blob_sets_status_without_fault(z):
         z.decompress_tensor(bad2, readback_to_cpu=True)
     # The context is still usable.
     assert torch.equal(z.decompress_tensor(blob).view(torch.int16), x.view(torch.int16))
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32", "float16"])
+def test_raw_planes_in_place_guess_right_and_wrong(z, dtype):
+    """The encoder writes skipped (raw) planes straight to the blob place they have when every
+    chunk codes one plane; the guess fails when some chunks code none (random bits) or more.
+    Either way the blob equals the oracle's."""
+    g = torch.Generator().manual_seed(3)
+    C = 16384
+    normal = (torch.randn(6 * C, generator=g) * 0.02).to(_TORCH[dtype])
+    noise = torch.randint(0, 256, (6 * C * normal.element_size(),), generator=g, dtype=torch.uint8).view(_TORCH[dtype])
+    zeros = torch.zeros(3 * C, dtype=_TORCH[dtype])
+    cases = {"all normal": normal, "noise chunks": torch.cat([normal[: 3 * C], noise[: 2 * C], normal[3 * C :]]),
+             "zero chunks": torch.cat([zeros, normal[:C + 5]])}
+    for name, x in cases.items():
+        ref = O.compress(_u8(x), x.shape, dtype, chunk_bytes=C, min_compress_bytes=0, threads=8)
+        blob = z.compress_tensor(x.cuda(), chunk_bytes=C, min_compress_bytes=0)
+        assert np.array_equal(_u8(blob), np.frombuffer(ref, dtype=np.uint8)), name
+        assert np.array_equal(_u8(z.decompress_tensor(blob)), _u8(x)), name
