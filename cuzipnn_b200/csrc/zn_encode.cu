@@ -215,19 +215,46 @@ __device__ __forceinline__ void plane_symbols(const uint8_t* xc, int64_t e0, int
 // Each thread keeps kHistDepth independent vector loads in flight before its atomics.
 constexpr int kHistDepth = 4;
 
+// Histogram layout for K <= 2: byte offset sym << 8 | plane << 7 | lane << 2 (lane = threadIdx % 32),
+// 64 KiB.  Every lane counts into its own column, so a warp's 32 atomics hit 32 different banks, and
+// one byte permute builds the offset from the symbol byte and the lane's column byte.  K >= 4 keeps
+// the [plane][sym][kCols] layout of 32-bit counters.
+constexpr int kHist32Bytes = 256 * 256;
+
+template <int KB>
+__device__ __forceinline__ void hist32_add(uint8_t* hist, uint32_t src, uint32_t colw) {
+  // Result bytes: [colw.b0, src.b(KB), 0, 0].
+  const uint32_t off = __byte_perm(src, colw, 0x5504u | (uint32_t(KB) << 4));
+  atomicAdd(reinterpret_cast<uint32_t*>(hist + off), 1u);
+}
+
 template <int K, bool REORDER, int VB>
 __device__ __forceinline__ void hist_count(uint32_t (&w)[VB / 4], uint32_t* hist, int col) {
-  if constexpr (K == 2 && REORDER) {
-    // bf16 (two elements per word): exponent bytes (u >> 7) & 0xFF at bytes 0 and 2 of w >> 7,
-    // sign / mantissa bytes (u >> 8 & 0x80) | (u & 0x7F) at bytes 0 and 2 of v.
+  if constexpr (K <= 2) {
+    uint8_t* h8 = reinterpret_cast<uint8_t*>(hist);
+    const uint32_t c0 = uint32_t(col) << 2, c1 = c0 | 128u;  // column bytes of planes 0 and 1
 #pragma unroll
     for (int q = 0; q < VB / 4; ++q) {
-      const uint32_t t = w[q] >> 7;
-      const uint32_t v = (w[q] & 0x007F007Fu) | ((w[q] >> 8) & 0x00800080u);
-      atomicAdd(&hist[(v & 0xFF) * kCols + col], 1u);
-      atomicAdd(&hist[(256 + (t & 0xFF)) * kCols + col], 1u);
-      atomicAdd(&hist[((v >> 16) & 0xFF) * kCols + col], 1u);
-      atomicAdd(&hist[(256 + ((t >> 16) & 0xFF)) * kCols + col], 1u);
+      if constexpr (K == 2 && REORDER) {
+        // bf16, two elements per word: exponent bytes (u >> 7) & 0xFF at bytes 0 and 2 of t,
+        // sign / mantissa bytes (u >> 8 & 0x80) | (u & 0x7F) at bytes 0 and 2 of v.
+        const uint32_t t = w[q] >> 7;
+        const uint32_t v = (w[q] & 0x007F007Fu) | ((w[q] >> 8) & 0x00800080u);
+        hist32_add<0>(h8, v, c0);
+        hist32_add<0>(h8, t, c1);
+        hist32_add<2>(h8, v, c0);
+        hist32_add<2>(h8, t, c1);
+      } else if constexpr (K == 2) {
+        hist32_add<0>(h8, w[q], c0);
+        hist32_add<1>(h8, w[q], c1);
+        hist32_add<2>(h8, w[q], c0);
+        hist32_add<3>(h8, w[q], c1);
+      } else {
+        hist32_add<0>(h8, w[q], c0);
+        hist32_add<1>(h8, w[q], c0);
+        hist32_add<2>(h8, w[q], c0);
+        hist32_add<3>(h8, w[q], c0);
+      }
     }
   } else {
     reorder_words<K, REORDER, true>(w, VB / 4);
@@ -276,7 +303,7 @@ __device__ __forceinline__ int64_t hist_vectors(const uint8_t* xc, int64_t m, ui
 template <int K, bool REORDER>
 __global__ void __launch_bounds__(kHistThreads) hist_kernel(const EncArgs* __restrict__ jobs, int njobs) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem_raw);  // [K][256][kCols]
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem_raw);  // K <= 2: kHist32Bytes layout; else [K][256][kCols]
   const EncArgs& a = jobs[find_job(jobs, njobs, blockIdx.x)];
   const int64_t j = blockIdx.x - a.chunk0;
   const int part = blockIdx.y, tid = threadIdx.x;
@@ -294,25 +321,36 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const EncArgs* __res
   const int64_t e0 = min(m, part * per), e1 = min(m, e0 + per);
   const uint8_t* xs = xc + e0 * K;
   const int64_t ms = e1 - e0;
-  for (int i = tid; i < K * 256 * kCols; i += kHistThreads) hist[i] = 0;
+  constexpr int kWords = K <= 2 ? kHist32Bytes / 4 : K * 256 * kCols;
+  for (int i = tid; i < kWords; i += kHistThreads) hist[i] = 0;
   __syncthreads();
   const uintptr_t xa = reinterpret_cast<uintptr_t>(xs);
   const int mode = (xa & 15) == 0 ? 2 : (xa & 7) == 0 ? 1 : 0;
-  const int col = tid & (kCols - 1);
+  const int col = K <= 2 ? (tid & 31) : (tid & (kCols - 1));
   int64_t done = 0;
   if (mode == 2) done = hist_vectors<K, REORDER, 16>(xs, ms, hist, col);
   else if (mode == 1) done = hist_vectors<K, REORDER, 8>(xs, ms, hist, col);
   for (int64_t e = done + tid; e < ms; e += kHistThreads) {
     const uint64_t u = reorder_elem<K, REORDER>(load_elem<K>(xs + e * K));
 #pragma unroll
-    for (int b = 0; b < K; ++b) atomicAdd(&hist[((b << 8) | uint32_t((u >> (8 * b)) & 0xFF)) * kCols + col], 1u);
+    for (int b = 0; b < K; ++b) {
+      const uint32_t byte = uint32_t((u >> (8 * b)) & 0xFF);
+      if constexpr (K <= 2) atomicAdd(&hist[(byte << 6) | (b << 5) | col], 1u);
+      else atomicAdd(&hist[((b << 8) | byte) * kCols + col], 1u);
+    }
   }
   __syncthreads();
   uint32_t* outp = a.part_hist + (j * kHistParts + part) * K * 256;
-  for (int i = tid; i < K * 256; i += kHistThreads) {
+  for (int i = tid; i < K * 256; i += kHistThreads) {  // i = plane * 256 + symbol
     uint32_t c = 0;
+    if constexpr (K <= 2) {
+      const uint32_t* h = hist + ((i & 255) << 6) + ((i >> 8) << 5);
 #pragma unroll
-    for (int q = 0; q < kCols; ++q) c += hist[i * kCols + ((q + i) & (kCols - 1))];
+      for (int q = 0; q < 32; ++q) c += h[(q + i) & 31];
+    } else {
+#pragma unroll
+      for (int q = 0; q < kCols; ++q) c += hist[i * kCols + ((q + i) & (kCols - 1))];
+    }
     outp[i] = c;
   }
 }
@@ -1084,7 +1122,7 @@ EncLayout enc_layout(int64_t units, int64_t C, int t) {
 }
 
 size_t enc_smem(int K) { return size_t(K) * 256 * 16 + sizeof(EncSmem); }
-size_t hist_smem(int K) { return size_t(K) * 256 * kCols * 4; }
+size_t hist_smem(int K) { return K <= 2 ? size_t(kHist32Bytes) : size_t(K) * 256 * kCols * 4; }
 
 
 int sub_log2(int sub_chunks) {
