@@ -66,9 +66,10 @@ struct EncArgs {
   uint8_t header[24 + 8 * 64];
 };
 
-// Parts per chunk of the histogram kernel: a chunk's histogram is built by kHistParts CTAs, so
-// the chunk is read at the full memory bandwidth rather than by one CTA.
-constexpr int kHistParts = 2;
+// Parts per chunk of the histogram kernel (CTAs per chunk, each writing a partial histogram that
+// the encoder sums).  One: with lane-private columns the counting keeps up, and fewer partial
+// histograms are written and read back.
+constexpr int kHistParts = 1;
 constexpr int kHistThreads = 256;
 
 struct EncSmem {
