@@ -631,7 +631,12 @@ __global__ void __launch_bounds__(kEncThreads, 7) encode_kernel(const EncArgs* _
     for (int c = 0; c < kEncChains; ++c)
       if (rounds > 0 && full_round(c, rounds - 1))
         load_words(xc + (base[c] + int64_t(rounds - 1) * kRound + l * kSteps) * K, nxt[c], 4 * K, mode == 2);
-    for (int r = rounds - 1; r >= 0; --r) {
+    // Rounds from the top; the partial rounds at the end of a sub-chunk come first, then the full
+    // rounds run the lean loop below (no predication, running pointers).
+    const int rfull = (kEncChains == 1 && mode != 0 && len[0] >= l * kSteps + kSteps)
+                          ? int((len[0] - l * kSteps - kSteps) / kRound) + 1 : 0;
+    int r = rounds - 1;
+    for (; r >= rfull; --r) {
       uint32_t sym[kEncChains][4];
       int nact[kEncChains];
 #pragma unroll
@@ -672,6 +677,34 @@ __global__ void __launch_bounds__(kEncThreads, 7) encode_kernel(const EncArgs* _
           flushed[c] -= 8;
           *reinterpret_cast<uint4*>(out[c] + flushed[c]) = S.stage[tid][(flushed[c] / 8) & 3];
         }
+    }
+    if constexpr (kEncChains == 1) {
+      const uint8_t* xp = xc + (base[0] + int64_t(r) * kRound + l * kSteps) * K;  // round r's elements
+      uint8_t* sp = spec_item ? spec0[0] + int64_t(r) * kRound : nullptr;
+      for (; r >= 0; --r) {
+        uint32_t sym[1][4];
+        plane_of_elements<K, REORDER>(nxt[0], b, sym[0]);
+        if (spec_item) {
+#pragma unroll
+          for (int q = 0; q < K; ++q) {
+            if (!((spec_mask >> q) & 1)) continue;
+            uint32_t raw[4];
+            plane_of_elements<K, REORDER>(nxt[0], q, raw);
+            uint2* d = reinterpret_cast<uint2*>(sp + q * a.spec_plane_bytes);
+            d[0] = make_uint2(raw[0], raw[1]);
+            d[1] = make_uint2(raw[2], raw[3]);
+          }
+        }
+        if (r > 0) load_words(xp - kRound * K, nxt[0], 4 * K, mode == 2);
+        const int nact[1] = {kSteps};
+        encode_round<true>(x, wp, stage, sym, tab, nact);
+        while (flushed[0] - wp[0] >= 8) {
+          flushed[0] -= 8;
+          *reinterpret_cast<uint4*>(out[0] + flushed[0]) = S.stage[tid][(flushed[0] / 8) & 3];
+        }
+        xp -= kRound * K;
+        if (spec_item) sp -= kRound;
+      }
     }
 #pragma unroll
     for (int c = 0; c < kEncChains; ++c)
