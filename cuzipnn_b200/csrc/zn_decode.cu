@@ -460,21 +460,29 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
       Cursor& cb = cur[0][0];
       uint4* ring = const_cast<uint4*>(reinterpret_cast<const uint4*>(ring16[0][0]));
       const uint32_t end8 = (cb.end + 7) & ~7u;
+      // Stream blocks [qbeg, qend) from gb lie wholly inside [lo, hi): one 16-byte load each.
+      const uint4* gb4 = reinterpret_cast<const uint4*>(gb[0]);
+      const uint32_t qbeg = gb[0] < lo[0] ? 1u : 0u;
+      const uint64_t span = hi[0] > gb[0] ? uint64_t(hi[0] - gb[0]) / 16 : 0;
+      const uint32_t qend = span > 0xFFFFFFFFull ? 0xFFFFFFFFu : uint32_t(span);
+      auto block = [&](uint32_t q) {
+        return q >= qbeg && q < qend ? __ldg(gb4 + q) : load_block(gb[0], q, lo[0], hi[0]);
+      };
       const uint8_t* rp[K];
 #pragma unroll
       for (int b = 0; b < K; ++b) rp[b] = src[b] + base[0] + l16;
       uint8_t* op = outc + (base[0] + l16) * K;  // 16-byte aligned when outc is (full rounds)
       for (; r < rfull; ++r) {
         if (ncoded > 0) {
+          // [ptr, ptr + 16) must be present (synchronous loads only when the ring ran low), then
+          // at most one block is fetched ahead per round, stored at the round's end.
           const uint32_t need = min((cb.ptr + 16 + 7) & ~7u, end8);
           while (cb.fill < need) {
-            ring[(cb.fill / 8) & (RH / 8 - 1)] = load_block(gb[0], cb.fill / 8, lo[0], hi[0]);
+            ring[(cb.fill / 8) & (RH / 8 - 1)] = block(cb.fill / 8);
             cb.fill += 8;
           }
-          const uint32_t limit = min((cb.ptr + RH) & ~7u, end8);
-          cb.nload = limit > cb.fill ? min((limit - cb.fill) / 8, 2u) : 0u;
-          if (cb.nload > 0) cb.r0 = load_block(gb[0], cb.fill / 8, lo[0], hi[0]);
-          if (cb.nload > 1) cb.r1 = load_block(gb[0], cb.fill / 8 + 1, lo[0], hi[0]);
+          cb.nload = cb.fill < end8 && cb.fill + 8 <= cb.ptr + RH ? 1u : 0u;
+          if (cb.nload) cb.r0 = block(cb.fill / 8);
         }
         uint32_t p[K][4];
 #pragma unroll
@@ -502,8 +510,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
 #pragma unroll
               for (int i = 0; i < 4; ++i) p[b][i] = acc[0][i];
             }
-          if (cb.nload > 0) ring[(cb.fill / 8) & (RH / 8 - 1)] = cb.r0;
-          if (cb.nload > 1) ring[(cb.fill / 8 + 1) & (RH / 8 - 1)] = cb.r1;
+          if (cb.nload) ring[(cb.fill / 8) & (RH / 8 - 1)] = cb.r0;
           cb.fill += 8 * cb.nload;
         }
         uint32_t e[4 * K];
