@@ -10,7 +10,18 @@ from ._codec import (
     hash_tensor_with_crc32,
     last_decode_status,
 )
-from ._shard import compress_shard, decompress_shard, gather_index, plan_shards
+from ._shard import (
+    assemble_chunk_ranges,
+    compress_chunk_range,
+    compress_shard,
+    decompress_chunk_range,
+    decompress_shard,
+    gather_chunk_ranges,
+    gather_index,
+    plan_chunk_ranges,
+    plan_shards,
+    split_chunk_range,
+)
 
 __all__ = [
     "compress_tensor",
@@ -24,4 +35,10 @@ __all__ = [
     "compress_shard",
     "decompress_shard",
     "gather_index",
+    "plan_chunk_ranges",
+    "compress_chunk_range",
+    "gather_chunk_ranges",
+    "assemble_chunk_ranges",
+    "split_chunk_range",
+    "decompress_chunk_range",
 ]
