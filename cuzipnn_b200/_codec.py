@@ -474,6 +474,7 @@ def _ptr_array(ctype, values):
 
 _PIPELINE_BYTES = 1 << 29  # sub-batch of host-resident inputs (upload overlapped with the kernels)
 _DEVICE_BATCH_BYTES = 1 << 31  # sub-batch of device-resident inputs (launched while the host prepares the next)
+_FIRST_BATCH_BYTES = 1 << 28  # the first sub-batch of a call is smaller, so that the GPU starts sooner
 _TINY_BYTES = 65536  # stored tensors up to this size decode into views of one shared buffer per call
 _COPY_BATCH_MAX = 1 << 29  # largest single copy of one zn_copy_chunks launch (65535 tiles of 8 KiB)
 
@@ -614,7 +615,8 @@ def compress_tensors(
         cur_bytes = 0
         for i in idx:
             nb = tensors[i].numel() * k
-            if cur and cur_bytes + nb > (_PIPELINE_BYTES if host_inputs else _DEVICE_BATCH_BYTES):
+            limit = _PIPELINE_BYTES if host_inputs else _DEVICE_BATCH_BYTES
+            if cur and cur_bytes + nb > (min(limit, _FIRST_BATCH_BYTES) if not batches else limit):
                 batches.append((k, reorder, cur))
                 cur, cur_bytes = [], 0
             cur.append(i)
@@ -863,7 +865,8 @@ def decompress_tensors(
         items, nbytes = cur.get(key, ([], 0))
         items.append((i, (dtype, shape, chunk_bytes, n_comp, n)))
         nbytes += blob.numel()
-        if nbytes >= (_PIPELINE_BYTES if not blob.is_cuda else _DEVICE_BATCH_BYTES):
+        limit = _PIPELINE_BYTES if not blob.is_cuda else _DEVICE_BATCH_BYTES
+        if nbytes >= (min(limit, _FIRST_BATCH_BYTES) if pos == 0 else limit):
             with torch.cuda.device(device):
                 launch(key[0], key[1], items)
             items, nbytes = [], 0

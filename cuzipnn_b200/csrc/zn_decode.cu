@@ -13,6 +13,7 @@
 // Every blob access is bounds-checked; a malformed unit raises a bit in the status word and its
 // elements are zeroed.  No wait in these kernels depends on another thread's progress except
 // __syncthreads().
+#include <type_traits>
 #include <vector>
 
 #include "zn_common.cuh"
@@ -199,22 +200,39 @@ __device__ __forceinline__ uint4 load_block(const uint8_t* gb, uint32_t q, const
 
 // Decoder state of one rANS state (a lane of a sub-chunk) of one coded plane.  Stream positions
 // are halfword indices relative to the 16-byte aligned base gb of the payload.  Each state keeps
-// a ring of RH halfwords of its stream in shared memory: at every round start [ptr, ptr + 16) is
-// present (a round consumes at most 16 words) and up to two 16-byte blocks ahead are loaded, to
-// be stored at the round's end.
+// a ring of kRing words of its stream in shared memory: at every round start [ptr, ptr + 16) is
+// present (a round consumes at most 16 words) and 16-byte blocks ahead are loaded, to be stored
+// at the round's end.
 struct Cursor {
   uint32_t x, ptr, end, fill, nload;
   uint4 r0, r1;
 };
 
-// Halfwords per ring: 64, or 32 when 8 coded planes share the shared memory.
+// Ring layout: slot p of the state of thread t sits at rings[(p % kRing) * kDecThreads + t] (rows
+// of kDecThreads slots), so the 32 states of a warp read their next words from 32 different banks
+// when a slot is 32 bits wide (one stream halfword in its low half; the decoder ignores the upper
+// half).  With more than 4 coded planes in shared memory the slots are halfwords (at most two
+// lanes per bank).
+constexpr int kRing = 32;
 template <int KC>
-__host__ __device__ constexpr int ring_half() { return KC > 4 ? 32 : 64; }
+using RingSlot = std::conditional_t<(KC > 4), uint16_t, uint32_t>;
+
+// Store the 16-byte stream block that starts at halfword `fill` (a multiple of 8) into a ring.
+template <typename Slot>
+__device__ __forceinline__ void ring_put(Slot* ring, uint32_t fill, const uint4& v) {
+  Slot* r = ring + (fill & (kRing - 1)) * kDecThreads;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    r[(2 * i) * kDecThreads] = Slot(w[i]);
+    r[(2 * i + 1) * kDecThreads] = Slot(w[i] >> 16);
+  }
+}
 
 // One decode step of one state (symbol into byte (i & 3) of acc, next word read one step ahead).
-template <bool FULL, int RH, int I>
+template <bool FULL, int I, typename Slot>
 __device__ __forceinline__ void decode_step(uint32_t& xv, uint32_t& pv, uint32_t& wn, uint32_t& acc, bool act,
-                                            const uint32_t* __restrict__ tab, const uint16_t* ring16) {
+                                            const uint32_t* __restrict__ tab, const Slot* ring) {
   const uint32_t e = tab[xv & (kM - 1)];
   const uint32_t q = xv >> kScaleBits;
   uint32_t xn = (e >> 20) * q + (q + (e & 0xFFFu));
@@ -223,26 +241,26 @@ __device__ __forceinline__ void decode_step(uint32_t& xv, uint32_t& pv, uint32_t
   const bool need = (FULL || act) && xn < kL;
   const uint32_t w = wn;
   pv += need;
-  wn = ring16[pv & (RH - 1)];
-  xv = need ? __byte_perm(w, xn, 0x5410) : xn;  // (xn << 16) | w
+  wn = ring[(pv & (kRing - 1)) * kDecThreads];
+  xv = need ? __byte_perm(w, xn, 0x5410) : xn;  // (xn << 16) | (w & 0xFFFF)
 }
 
 // 16 steps of the lane's kChains states, interleaved so the independent chains overlap.  A stream
 // over-read is not tested per step: it leaves the final state or position wrong, which the caller
 // checks (ring reads are always in bounds).
-template <bool FULL, int RH>
-__device__ __forceinline__ void decode_round(Cursor* cb, const uint32_t* __restrict__ tab, const uint16_t* const* ring16,
+template <bool FULL, typename Slot>
+__device__ __forceinline__ void decode_round(Cursor* cb, const uint32_t* __restrict__ tab, Slot* const* ring,
                                              const int* nact, uint32_t (*acc)[4]) {
   uint32_t xv[kChains], pv[kChains], wn[kChains];
 #pragma unroll
   for (int c = 0; c < kChains; ++c) {
     xv[c] = cb[c].x;
     pv[c] = cb[c].ptr;
-    wn[c] = ring16[c][pv[c] & (RH - 1)];
+    wn[c] = ring[c][(pv[c] & (kRing - 1)) * kDecThreads];
   }
 #define ZN_STEP(I)                                                                                    \
   _Pragma("unroll") for (int c = 0; c < kChains; ++c)                                                 \
-      decode_step<FULL, RH, I>(xv[c], pv[c], wn[c], acc[c][(I) >> 2], (I) < nact[c], tab, ring16[c]);
+      decode_step<FULL, I>(xv[c], pv[c], wn[c], acc[c][(I) >> 2], (I) < nact[c], tab, ring[c]);
   ZN_STEP(0) ZN_STEP(1) ZN_STEP(2) ZN_STEP(3) ZN_STEP(4) ZN_STEP(5) ZN_STEP(6) ZN_STEP(7)
   ZN_STEP(8) ZN_STEP(9) ZN_STEP(10) ZN_STEP(11) ZN_STEP(12) ZN_STEP(13) ZN_STEP(14) ZN_STEP(15)
 #undef ZN_STEP
@@ -311,10 +329,10 @@ __device__ __forceinline__ void assemble_elements(const uint32_t (*p)[4], uint32
 template <int K, bool REORDER, int KC>
 __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __restrict__ jobs, int njobs, bool overflow_pass) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  constexpr int RH = ring_half<KC>();
+  using Slot = RingSlot<KC>;
   uint32_t* tabs = reinterpret_cast<uint32_t*>(smem_raw);                      // [KC][4096]
-  uint4* rings = reinterpret_cast<uint4*>(smem_raw + KC * kM * 4);             // [KC][kChains][threads][RH / 8]
-  DecSmem& S = *reinterpret_cast<DecSmem*>(smem_raw + KC * kM * 4 + KC * kChains * kDecThreads * RH * 2);
+  Slot* rings = reinterpret_cast<Slot*>(smem_raw + KC * kM * 4);                // [KC][kChains][kRing][threads]
+  DecSmem& S = *reinterpret_cast<DecSmem*>(smem_raw + KC * kM * 4 + KC * kChains * kRing * kDecThreads * sizeof(Slot));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const DecArgs& a = jobs[find_job(jobs, njobs, blockIdx.x)];
   const int64_t j = blockIdx.x - a.chunk0;
@@ -420,13 +438,13 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
       len[c] = valid[c] ? min(g.sc, m - base[c]) : 0;
     }
     Cursor cur[KC][kChains];
-    const uint16_t* ring16[KC][kChains];
+    Slot* ring[KC][kChains];
 #pragma unroll
     for (int q = 0; q < KC; ++q)
 #pragma unroll
       for (int c = 0; c < kChains; ++c) {
         Cursor& cb = cur[q][c];
-        ring16[q][c] = reinterpret_cast<const uint16_t*>(rings + ((q * kChains + c) * kDecThreads + tid) * (RH / 8));
+        ring[q][c] = rings + (q * kChains + c) * kRing * kDecThreads + tid;
         cb.x = kL;
         cb.ptr = cb.end = cb.fill = cb.nload = 0;
         if (q < ncoded && valid[c]) {
@@ -458,7 +476,6 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
       const int64_t l16 = int64_t(l) * kSteps;
       const int rfull = len[0] >= l16 + kSteps ? int((len[0] - l16 - kSteps) / kRound) + 1 : 0;
       Cursor& cb = cur[0][0];
-      uint4* ring = const_cast<uint4*>(reinterpret_cast<const uint4*>(ring16[0][0]));
       const uint32_t end8 = (cb.end + 7) & ~7u;
       // Stream blocks [qbeg, qend) from gb lie wholly inside [lo, hi): one 16-byte load each.
       const uint4* gb4 = reinterpret_cast<const uint4*>(gb[0]);
@@ -478,10 +495,10 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
           // at most one block is fetched ahead per round, stored at the round's end.
           const uint32_t need = min((cb.ptr + 16 + 7) & ~7u, end8);
           while (cb.fill < need) {
-            ring[(cb.fill / 8) & (RH / 8 - 1)] = block(cb.fill / 8);
+            ring_put(ring[0][0], cb.fill, block(cb.fill / 8));
             cb.fill += 8;
           }
-          cb.nload = cb.fill < end8 && cb.fill + 8 <= cb.ptr + RH ? 1u : 0u;
+          cb.nload = cb.fill < end8 && cb.fill + 8 <= cb.ptr + kRing ? 1u : 0u;
           if (cb.nload) cb.r0 = block(cb.fill / 8);
         }
         uint32_t p[K][4];
@@ -503,14 +520,14 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
         if (ncoded > 0) {
           int nact[1] = {kSteps};
           uint32_t acc[1][4] = {};
-          decode_round<true, RH>(cur[0], tabs, ring16[0], nact, acc);
+          decode_round<true>(cur[0], tabs, ring[0], nact, acc);
 #pragma unroll
           for (int b = 0; b < K; ++b)
             if (b == pslot[0]) {
 #pragma unroll
               for (int i = 0; i < 4; ++i) p[b][i] = acc[0][i];
             }
-          if (cb.nload) ring[(cb.fill / 8) & (RH / 8 - 1)] = cb.r0;
+          if (cb.nload) ring_put(ring[0][0], cb.fill, cb.r0);
           cb.fill += 8 * cb.nload;
         }
         uint32_t e[4 * K];
@@ -536,14 +553,13 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
 #pragma unroll
         for (int c = 0; c < kChains; ++c) {
           Cursor& cb = cur[q][c];
-          uint4* ring = const_cast<uint4*>(reinterpret_cast<const uint4*>(ring16[q][c]));
           const uint32_t end8 = (cb.end + 7) & ~7u;
           const uint32_t need = min((cb.ptr + 16 + 7) & ~7u, end8);
           while (cb.fill < need) {
-            ring[(cb.fill / 8) & (RH / 8 - 1)] = load_block(gb[q], cb.fill / 8, lo[q], hi[q]);
+            ring_put(ring[q][c], cb.fill, load_block(gb[q], cb.fill / 8, lo[q], hi[q]));
             cb.fill += 8;
           }
-          const uint32_t limit = min((cb.ptr + RH) & ~7u, end8);
+          const uint32_t limit = min((cb.ptr + kRing) & ~7u, end8);
           cb.nload = limit > cb.fill ? min((limit - cb.fill) / 8, 2u) : 0u;
           if (cb.nload > 0) cb.r0 = load_block(gb[q], cb.fill / 8, lo[q], hi[q]);
           if (cb.nload > 1) cb.r1 = load_block(gb[q], cb.fill / 8 + 1, lo[q], hi[q]);
@@ -564,8 +580,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
       for (int q = 0; q < KC; ++q) {
         if (q >= ncoded) break;
         uint32_t acc[kChains][4] = {};
-        if (full) decode_round<true, RH>(cur[q], tabs + q * kM, ring16[q], nact, acc);
-        else decode_round<false, RH>(cur[q], tabs + q * kM, ring16[q], nact, acc);
+        if (full) decode_round<true>(cur[q], tabs + q * kM, ring[q], nact, acc);
+        else decode_round<false>(cur[q], tabs + q * kM, ring[q], nact, acc);
 #pragma unroll
         for (int c = 0; c < kChains; ++c)
 #pragma unroll
@@ -582,9 +598,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
 #pragma unroll
         for (int c = 0; c < kChains; ++c) {
           Cursor& cb = cur[q][c];
-          uint4* ring = const_cast<uint4*>(reinterpret_cast<const uint4*>(ring16[q][c]));
-          if (cb.nload > 0) ring[(cb.fill / 8) & (RH / 8 - 1)] = cb.r0;
-          if (cb.nload > 1) ring[(cb.fill / 8 + 1) & (RH / 8 - 1)] = cb.r1;
+          if (cb.nload > 0) ring_put(ring[q][c], cb.fill, cb.r0);
+          if (cb.nload > 1) ring_put(ring[q][c], cb.fill + 8, cb.r1);
           cb.fill += 8 * cb.nload;
         }
       }
@@ -684,7 +699,7 @@ __global__ void __launch_bounds__(kScanThreads) dscan_kernel(const DecArgs* __re
 }
 
 size_t dec_smem(int KC) {
-  return size_t(KC) * kM * 4 + size_t(KC) * kChains * kDecThreads * (KC > 4 ? 32 : 64) * 2 + sizeof(DecSmem);
+  return size_t(KC) * kM * 4 + size_t(KC) * kChains * kRing * kDecThreads * (KC > 4 ? 2 : 4) + sizeof(DecSmem);
 }
 
 template <int K, bool REORDER, int KC>

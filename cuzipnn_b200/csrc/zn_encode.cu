@@ -81,7 +81,7 @@ struct EncSmem {
   int npl[8];
   int skip[8];
   int nwsum[8];             // stream words per plane
-  uint4 stage[kEncThreads][4];  // per lane: last 32 emitted words, flushed in 16-byte blocks
+  uint32_t stage[32][kEncThreads];  // per lane: last 32 emitted words, word h of lane t at [h % 32][t]
 };
 
 // ---- block-wide helpers (kEncThreads = 128 threads = 4 warps) ----------------------------------
@@ -359,25 +359,35 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const EncArgs* __res
 // One encode step of one state for symbol byte I (last symbol first; the decoder runs forward).
 // A state at or above f * 2^19 (it would leave [L, 2^31) after coding) emits its low 16 bits into
 // its own stream, which grows down from the end of the state's slot; the word goes to the lane's
-// 32-halfword staging ring in shared memory (one predicated 2-byte store, no branch).  Then
+// 32-word staging ring in shared memory (one predicated store of x, whose low half is the word, no
+// branch; the rings interleave by lane, so every lane of a warp stores to its own bank).  Then
 // x' = x + bias + q * (M - f) with q = floor(x / f) = umulhi(x, magic) >> shift, exact because
 // x < 2^31; the shift sits in the low 5 bits of e.z, which the wrapping funnel shift uses.
 template <bool FULL, int I>
-__device__ __forceinline__ void encode_step(uint32_t& x, uint32_t& wp, uint16_t* stage, const uint32_t* sym,
+__device__ __forceinline__ void encode_step(uint32_t& x, uint32_t& wp, uint32_t* stage, const uint32_t* sym,
                                             const uint4* tab, bool act) {
   const uint4 e = tab[get_byte(sym, I)];  // {magic, bias, (M - f) << 5 | shift, f * 2^19 - 1}
   const bool emit = (FULL || act) && x > e.w;
   wp -= emit;
-  if (emit) stage[wp & 31] = uint16_t(x);
+  if (emit) stage[(wp & 31) * kEncThreads] = x;
   x = emit ? x >> 16 : x;
   const uint32_t q = __funnelshift_r(__umulhi(x, e.x), 0u, e.z);
   const uint32_t xn = x + e.y + q * (e.z >> 5);
   x = (FULL || act) ? xn : x;
 }
 
+// The 16-byte stream block of words h .. h + 7 (h a multiple of 8) from a lane's staging ring.
+__device__ __forceinline__ uint4 stage_block(const uint32_t* st, uint32_t h) {
+  const uint32_t* s = st + (h & 31) * kEncThreads;
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = __byte_perm(s[2 * i * kEncThreads], s[(2 * i + 1) * kEncThreads], 0x5410);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 // 16 steps of the lane's kEncChains states, interleaved so the independent chains overlap.
 template <bool FULL>
-__device__ __forceinline__ void encode_round(uint32_t* x, uint32_t* wp, uint16_t* const* stage,
+__device__ __forceinline__ void encode_round(uint32_t* x, uint32_t* wp, uint32_t* const* stage,
                                              const uint32_t (*sym)[4], const uint4* tab, const int* nact) {
 #define ZN_ESTEP(I)                                                                                   \
   _Pragma("unroll") for (int c = 0; c < kEncChains; ++c)                                              \
@@ -606,7 +616,7 @@ __global__ void __launch_bounds__(kEncThreads, 7) encode_kernel(const EncArgs* _
     bool valid[kEncChains];
     int64_t base[kEncChains], len[kEncChains];
     uint16_t* out[kEncChains];
-    uint16_t* stage[kEncChains];
+    uint32_t* stage[kEncChains];
     uint32_t x[kEncChains], wp[kEncChains], flushed[kEncChains];
     uint32_t nxt[kEncChains][4 * K];
     uint8_t* spec0[kEncChains];  // this lane's bytes of plane 0 at the guessed blob place
@@ -620,7 +630,7 @@ __global__ void __launch_bounds__(kEncThreads, 7) encode_kernel(const EncArgs* _
       out[c] = a.streams + u * a.unit_words + int64_t(gi[c]) * a.sub_words + int64_t(l) * a.lane_words;
       x[c] = kL;
       wp[c] = flushed[c] = uint32_t(a.lane_words);  // the stream grows down from the slot's end
-      stage[c] = reinterpret_cast<uint16_t*>(S.stage[tid]);  // one ring per lane: kEncChains == 1
+      stage[c] = &S.stage[0][tid];  // one ring per lane: kEncChains == 1
       spec0[c] = spec_item ? a.out + a.spec_data_off + j * align8(a.C) + base[c] + l * kSteps : nullptr;
     }
     // The elements of the next (lower) round are loaded while the current round is encoded.
@@ -675,7 +685,7 @@ __global__ void __launch_bounds__(kEncThreads, 7) encode_kernel(const EncArgs* _
       for (int c = 0; c < kEncChains; ++c)
         while (flushed[c] - wp[c] >= 8) {
           flushed[c] -= 8;
-          *reinterpret_cast<uint4*>(out[c] + flushed[c]) = S.stage[tid][(flushed[c] / 8) & 3];
+          *reinterpret_cast<uint4*>(out[c] + flushed[c]) = stage_block(stage[c], flushed[c]);
         }
     }
     if constexpr (kEncChains == 1) {
@@ -700,7 +710,7 @@ __global__ void __launch_bounds__(kEncThreads, 7) encode_kernel(const EncArgs* _
         encode_round<true>(x, wp, stage, sym, tab, nact);
         while (flushed[0] - wp[0] >= 8) {
           flushed[0] -= 8;
-          *reinterpret_cast<uint4*>(out[0] + flushed[0]) = S.stage[tid][(flushed[0] / 8) & 3];
+          *reinterpret_cast<uint4*>(out[0] + flushed[0]) = stage_block(stage[0], flushed[0]);
         }
         xp -= kRound * K;
         if (spec_item) sp -= kRound;
@@ -708,7 +718,7 @@ __global__ void __launch_bounds__(kEncThreads, 7) encode_kernel(const EncArgs* _
     }
 #pragma unroll
     for (int c = 0; c < kEncChains; ++c)
-      for (uint32_t h = wp[c]; h < flushed[c]; ++h) out[c][h] = stage[c][h & 31];
+      for (uint32_t h = wp[c]; h < flushed[c]; ++h) out[c][h] = uint16_t(stage[c][(h & 31) * kEncThreads]);
 #pragma unroll
     for (int c = 0; c < kEncChains; ++c) {
       if (!valid[c]) continue;
