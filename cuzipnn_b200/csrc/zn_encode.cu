@@ -887,6 +887,11 @@ __device__ __forceinline__ uint4 shift_blocks(const uint4& A, const uint4& B, ui
   }
 }
 
+// Copy L bytes (even; dst and src 2-byte aligned) by G cooperating lanes (lane in [0, G), G >= 8 so
+// that the head and the tail, at most 7 halfwords each, take one store per lane): halfword stores
+// up to dst's 16-byte boundary, then 16-byte stores of the source shifted into place, then the
+// tail.  Writes exactly [dst, dst + L).
+template <int G = 32>
 __device__ __forceinline__ void warp_copy16(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, int64_t L,
                                             int lane) {
   const int64_t h = min(L, int64_t((16 - (reinterpret_cast<uintptr_t>(dst) & 15)) & 15));
@@ -897,7 +902,7 @@ __device__ __forceinline__ void warp_copy16(uint8_t* __restrict__ dst, const uin
   const uint4* sa = reinterpret_cast<const uint4*>(s - r);
   uint4* d = reinterpret_cast<uint4*>(dst + h);
   const uint32_t q = r >> 2, sh = (r & 3) * 8;
-  for (int64_t k = lane; k < nb; k += 32) {
+  for (int64_t k = lane; k < nb; k += G) {
     const uint4 A = sa[k];
     d[k] = r ? shift_blocks(A, sa[k + 1], q, sh) : A;
   }
@@ -928,7 +933,7 @@ __device__ void block_scan_pairs(int32_t v0, int32_t v1, int32_t* out, int32_t* 
 }
 
 // Shared-memory staging of the payload copy: 16-byte blocks, filled by cp.async.
-constexpr int kStageBlocks = 1024;  // 16 KiB
+constexpr int kStageBlocks = 2048;  // 32 KiB
 
 struct PayloadSmem {
   int32_t pre[2 * kPackThreads + 1];   // stream start, halfwords after the meta block
@@ -985,25 +990,24 @@ __device__ void copy_payload(const EncArgs& a, uint64_t u, int64_t m, uint8_t* d
       const int32_t n = P.pre[fa + 1] - P.pre[fa];
       if (warp == 0) warp_copy16(dst + 2 * (mh + int64_t(P.pre[fa])), src_of(fa, n), 2 * int64_t(n), lane);
     } else {
-      int span = 1;
-      while (span < fb - fa) span <<= 1;
-      for (int32_t jb = tid; jb < nb; jb += kPackThreads) {
-        int fi = fa;  // stream of staged block jb: largest fi in [fa, fb) with bpre[fi] <= b0 + jb
-        for (int st = span >> 1; st > 0; st >>= 1)
-          if (fi + st < fb && P.bpre[fi + st] <= b0 + jb) fi += st;
+      // Groups of 8 threads, one stream each: stage the stream's 16-byte blocks, then copy it out.
+      const int grp = tid >> 3, g8 = tid & 7;
+      for (int fi = fa + grp; fi < fb; fi += kPackThreads / 8) {
         const int32_t n = P.pre[fi + 1] - P.pre[fi];
+        if (!n) continue;
         const uint8_t* s0 = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(src_of(fi, n)) & ~uintptr_t(15));
-        cp_async16(&P.stage[jb], s0 + 16 * int64_t(b0 + jb - P.bpre[fi]));
+        const int32_t nbf = P.bpre[fi + 1] - P.bpre[fi];
+        for (int32_t k = g8; k < nbf; k += 8) cp_async16(&P.stage[P.bpre[fi] - b0 + k], s0 + 16 * int64_t(k));
       }
       asm volatile("cp.async.commit_group;\n" ::: "memory");
       asm volatile("cp.async.wait_group 0;\n" ::: "memory");
       __syncthreads();
-      for (int fi = fa + warp; fi < fb; fi += nwarps) {
+      for (int fi = fa + grp; fi < fb; fi += kPackThreads / 8) {
         const int32_t n = P.pre[fi + 1] - P.pre[fi];
         if (!n) continue;
         const uintptr_t off = reinterpret_cast<uintptr_t>(src_of(fi, n)) & 15;
-        warp_copy16(dst + 2 * (mh + int64_t(P.pre[fi])),
-                    reinterpret_cast<const uint8_t*>(&P.stage[P.bpre[fi] - b0]) + off, 2 * int64_t(n), lane);
+        warp_copy16<8>(dst + 2 * (mh + int64_t(P.pre[fi])),
+                       reinterpret_cast<const uint8_t*>(&P.stage[P.bpre[fi] - b0]) + off, 2 * int64_t(n), g8);
       }
     }
     __syncthreads();
