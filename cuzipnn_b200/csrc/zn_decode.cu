@@ -54,6 +54,7 @@ struct PlaneInfo {
   int64_t size;
   int coded;
   int t;
+  int single;              // the symbol of a plane with one symbol (f = M: no words, no state change), else -1
   int64_t states_off;
   int64_t lens_off;        // per-state stream lengths
   int lw;                  // bytes per length field
@@ -95,8 +96,10 @@ __device__ __forceinline__ uint32_t block_excl(uint32_t v, uint32_t* red) {
 }
 
 // Parse a ZNR2 payload header and build its decode table.  Entry of slot z (symbol s, cum c, freq
-// f): (f - 1) << 20 | s << 12 | (z - c), so the state update f * (x >> 12) + (z - c) is one IMAD
-// after the lookup.  Returns false (uniformly) if the payload is malformed.
+// f < M): f << 20 | s << 12 | (z - c), so the state update f * (x >> 12) + (z - c) is one IMAD
+// after the lookup.  A plane with a single symbol (f = M) needs no table: its state never changes
+// and it has no words; P.single holds that symbol.  Returns false (uniformly) if the payload is
+// malformed.
 __device__ bool build_plane(PlaneInfo& P, int64_t m, uint32_t* tab, DecSmem& S) {
   const int tid = threadIdx.x;
   const uint8_t* pl = P.pl;
@@ -132,6 +135,11 @@ __device__ bool build_plane(PlaneInfo& P, int64_t m, uint32_t* tab, DecSmem& S) 
   }
   const uint32_t total = block_sum(fsum, S.red);
   if (total != kM) return false;
+  if (np == 1) {
+#pragma unroll
+    for (int h = 0; h < kSym; ++h)
+      if (pres[h]) P.single = kSym * tid + h;
+  }
   uint32_t c0 = block_excl(fsum, S.red);
 #pragma unroll
   for (int h = 0; h < kSym; ++h) {
@@ -177,7 +185,7 @@ __device__ bool build_plane(PlaneInfo& P, int64_t m, uint32_t* tab, DecSmem& S) 
   const int lane = tid & 31, warp = tid >> 5;
   for (int s = warp; s < 256; s += kDecThreads / 32) {
     const uint32_t f = S.f[s], c = S.cum[s];
-    const uint32_t hi = ((f - 1) << 20) | (uint32_t(s) << 12);
+    const uint32_t hi = (f << 20) | (uint32_t(s) << 12);  // f = M (one symbol) wraps: the table is unused
     for (uint32_t q = lane; q < f; q += 32) tab[c + q] = hi | q;
   }
   __syncthreads();
@@ -235,7 +243,7 @@ __device__ __forceinline__ void decode_step(uint32_t& xv, uint32_t& pv, uint32_t
                                             const uint32_t* __restrict__ tab, const Slot* ring) {
   const uint32_t e = tab[xv & (kM - 1)];
   const uint32_t q = xv >> kScaleBits;
-  uint32_t xn = (e >> 20) * q + (q + (e & 0xFFFu));
+  uint32_t xn = (e >> 20) * q + (e & 0xFFFu);
   if (!FULL) xn = act ? xn : xv;
   acc = __byte_perm(acc, e >> 12, (0x3210 & ~(0xF << (4 * (I & 3)))) | (4 << (4 * (I & 3))));
   const bool need = (FULL || act) && xn < kL;
@@ -269,6 +277,14 @@ __device__ __forceinline__ void decode_round(Cursor* cb, const uint32_t* __restr
     cb[c].x = xv[c];
     cb[c].ptr = pv[c];
   }
+}
+
+// The 16 symbols of a round of a one-symbol plane, for every chain.
+__device__ __forceinline__ void fill_single(uint32_t (*acc)[4], int s) {
+#pragma unroll
+  for (int c = 0; c < kChains; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[c][i] = uint32_t(s) * 0x01010101u;
 }
 
 // Raw (stored) plane bytes of round r for each chain: 16 bytes per plane from the lane's 16
@@ -368,6 +384,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
       if (s < 0) atomicOr(&S.err, 1);
     }
     P.t = -1;
+    P.single = -1;
   }
   __syncthreads();
   int ncoded = 0;
@@ -439,6 +456,9 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
     }
     Cursor cur[KC][kChains];
     Slot* ring[KC][kChains];
+    int single[KC];  // symbol of a one-symbol coded plane, else -1
+#pragma unroll
+    for (int q = 0; q < KC; ++q) single[q] = q < ncoded ? S.p[pslot[q]].single : -1;
 #pragma unroll
     for (int q = 0; q < KC; ++q)
 #pragma unroll
@@ -520,7 +540,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
         if (ncoded > 0) {
           int nact[1] = {kSteps};
           uint32_t acc[1][4] = {};
-          decode_round<true>(cur[0], tabs, ring[0], nact, acc);
+          if (single[0] < 0) decode_round<true>(cur[0], tabs, ring[0], nact, acc);
+          else fill_single(acc, single[0]);
 #pragma unroll
           for (int b = 0; b < K; ++b)
             if (b == pslot[0]) {
@@ -580,7 +601,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
       for (int q = 0; q < KC; ++q) {
         if (q >= ncoded) break;
         uint32_t acc[kChains][4] = {};
-        if (full) decode_round<true>(cur[q], tabs + q * kM, ring[q], nact, acc);
+        if (single[q] >= 0) fill_single(acc, single[q]);
+        else if (full) decode_round<true>(cur[q], tabs + q * kM, ring[q], nact, acc);
         else decode_round<false>(cur[q], tabs + q * kM, ring[q], nact, acc);
 #pragma unroll
         for (int c = 0; c < kChains; ++c)
