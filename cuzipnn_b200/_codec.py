@@ -28,12 +28,14 @@ other versions (src/cuzipnn/_codec.py:423-424).
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import math
 import struct
 import zlib
 from collections.abc import Buffer
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -349,17 +351,20 @@ def _compress(
         return blob, None if crc is None else crc.cpu()
 
 
-def _parse_header(prefix: Buffer) -> tuple[torch.dtype, tuple[int, ...], int, int, int, int]:
-    """(_codec.py:416-428)"""
+def _parse_header(prefix: Buffer, off: int = 0, length: int | None = None
+                  ) -> tuple[torch.dtype, tuple[int, ...], int, int, int, int]:
+    """(_codec.py:416-428) The header in prefix[off : off + length] (default: to the end)."""
     prefix = memoryview(prefix)
-    if len(prefix) < _FIXED.size:
+    if length is None:
+        length = len(prefix) - off
+    if length < _FIXED.size:
         raise ValueError("blob is too short")
-    magic, version, code, ndim, flags, chunk_bytes, n_comp, n = _FIXED.unpack_from(prefix)
+    magic, version, code, ndim, flags, chunk_bytes, n_comp, n = _FIXED.unpack_from(prefix, off)
     if magic != _MAGIC or version != _VERSION or code not in _DTYPES:
         raise ValueError("not a cuzipnn blob")
-    if len(prefix) < _FIXED.size + 8 * ndim:
+    if length < _FIXED.size + 8 * ndim:
         raise ValueError("blob is too short")
-    shape = struct.unpack_from(f"<{ndim}q", prefix, _FIXED.size)
+    shape = struct.unpack_from(f"<{ndim}q", prefix, off + _FIXED.size)
     return _DTYPES[code], shape, flags, chunk_bytes, n_comp, n
 
 
@@ -497,7 +502,7 @@ def _copy_batch(device: torch.device, srcs: list[int], dsts: list[int], sizes: l
     n = len(srcs)
     if n == 0:
         return
-    host = torch.tensor(srcs + dsts + sizes, dtype=torch.int64).pin_memory()
+    host = torch.from_numpy(np.array(srcs + dsts + sizes, dtype=np.int64)).pin_memory()
     tbl = host.to(device, non_blocking=True)
     base = tbl.data_ptr()
     _lib.check(
@@ -557,28 +562,16 @@ def compress_tensors(
     With readback_to_cpu=False the blobs are views into one shared GPU buffer per batch.  Host
     inputs are uploaded in batches of about _PIPELINE_BYTES on a side stream, so that uploads,
     kernels and (with readback_to_cpu) downloads of different batches overlap; with pin_memory the
-    read-back blobs of a batch are views into one pinned buffer."""
+    read-back blobs of a batch are views into one pinned buffer.  Tensors are checked as the list
+    is read, so an invalid tensor raises after the batches before it may have been launched (their
+    results are dropped)."""
     blobs: list[torch.Tensor | None] = [None] * len(tensors)
-    groups: dict[tuple[int, bool], list[int]] = {}
     small: list[int] = []  # stored path and empty tensors, handled after the coded launches
     sub_chunks = _sub_chunks(chunk_bytes, sub_chunk_bytes) if sub_chunk_bytes > 0 else 0
-    for i, t in enumerate(tensors):
-        if i == 0:  # the scalar arguments once, then each tensor's dtype and rank
-            _, sub_chunks = _check_args(t, chunk_bytes, sub_chunk_bytes, passthrough_threshold, min_compress_bytes,
-                                        None, pin_memory, compute_device, readback_to_cpu)
-        elif t.dtype not in _CODES:
-            raise TypeError(f"unsupported dtype {t.dtype}")
-        elif t.dim() > _MAX_NDIM:
-            raise ValueError(f"at most {_MAX_NDIM} dimensions are supported")
-        k, n = t.element_size(), t.numel()
-        if n * k < min_compress_bytes or n == 0:
-            small.append(i)
-        else:
-            groups.setdefault((k, t.dtype in _REORDER), []).append(i)
+    cd = _check_device(compute_device)
 
     def compress_small(device: torch.device | None) -> None:
         batch = []
-        cd = _check_device(compute_device)
         for i in small:
             t = tensors[i]
             k, n = t.element_size(), t.numel()
@@ -596,71 +589,99 @@ def compress_tensors(
             for i, b in _stored_blobs_gpu(batch, device).items():
                 blobs[i] = b
 
-    if not groups:
-        if small and not readback_to_cpu:
-            device = _gpu(tensors[small[0]].detach(), _check_device(compute_device))
-            with torch.cuda.device(device):
-                compress_small(device)
-        else:
-            compress_small(None)
-        return blobs  # type: ignore[return-value]
-    first = tensors[next(iter(groups.values()))[0]]
-    device = _gpu(first.detach(), _check_device(compute_device))
-    # Host-resident inputs go up in sub-batches on a copy stream, so that the upload of one batch
-    # overlaps the kernels of the previous one (and, with readback, the download of the one before).
-    host_inputs = any(not tensors[i].is_cuda for idx in groups.values() for i in idx)
-    batches: list[tuple[int, bool, list[int]]] = []
-    for (k, reorder), idx in groups.items():
-        cur: list[int] = []
-        cur_bytes = 0
-        for i in idx:
-            nb = tensors[i].numel() * k
-            limit = _PIPELINE_BYTES if host_inputs else _DEVICE_BATCH_BYTES
-            if cur and cur_bytes + nb > (min(limit, _FIRST_BATCH_BYTES) if not batches else limit):
-                batches.append((k, reorder, cur))
-                cur, cur_bytes = [], 0
-            cur.append(i)
-            cur_bytes += nb
-        batches.append((k, reorder, cur))
-    pending = []
-    with torch.cuda.device(device):
-        stream = torch.cuda.current_stream(device)
-        copy_in = _side_stream(device, 0) if host_inputs else stream
-        for k, reorder, idx in batches:
-            with torch.cuda.stream(copy_in):
-                xs = []
-                for i in idx:
-                    x = tensors[i].detach()
-                    if not (x.device == device and x.is_contiguous() and x.data_ptr() % 16 == 0):
-                        x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
-                        if x.data_ptr() % 16:
-                            x = x.clone()
-                    xs.append(x.view(-1))
-            if copy_in is not stream:
-                stream.wait_stream(copy_in)
-                for x in xs:
-                    x.record_stream(stream)
-            out, offs, sizes, temp = _launch_compress_batch(
-                device, xs, [tensors[i] for i in idx], k, reorder, chunk_bytes, sub_chunks, passthrough_threshold)
-            sizes_host = None
-            if readback_to_cpu:  # each batch's sizes come back on their own, batches keep running
-                sizes_host = torch.empty(len(idx), dtype=torch.int64, pin_memory=True)
-                sizes_host.copy_(sizes, non_blocking=True)
-            done = torch.cuda.Event()
-            done.record(stream)
-            # The staged inputs and the scratch are only used on `stream` from here on, so the
-            # caching allocator may hand their memory to later batches in stream order.
-            del xs, temp
-            pending.append([idx, out, offs, sizes, sizes_host, done])
+    device: torch.device | None = None
+    stream = copy_in = None
+    pending: list[list] = []
+
+    def launch(k: int, reorder: bool, idx: list[int]) -> None:
+        """Stage a batch's inputs on the device (host tensors go up on the copy stream, so that the
+        upload of one batch overlaps the kernels of the previous one) and launch its kernels."""
+        nonlocal copy_in
+        host = any(not tensors[i].is_cuda for i in idx)
+        if host and copy_in is None:
+            copy_in = _side_stream(device, 0)
+        up = copy_in if host else stream
+        with torch.cuda.stream(up):
+            xs = []
+            for i in idx:
+                x = tensors[i].detach()
+                if not (x.device == device and x.is_contiguous() and x.data_ptr() % 16 == 0):
+                    x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+                    if x.data_ptr() % 16:
+                        x = x.clone()
+                xs.append(x.view(-1))
+        if up is not stream:
+            stream.wait_stream(up)
+            for x in xs:
+                x.record_stream(stream)
+        out, offs, sizes, temp = _launch_compress_batch(
+            device, xs, [tensors[i] for i in idx], k, reorder, chunk_bytes, sub_chunks, passthrough_threshold)
+        sizes_host = None
+        if readback_to_cpu:  # each batch's sizes come back on their own, batches keep running
+            sizes_host = torch.empty(len(idx), dtype=torch.int64, pin_memory=True)
+            sizes_host.copy_(sizes, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(stream)
+        # The staged inputs and the scratch are only used on `stream` from here on, so the
+        # caching allocator may hand their memory to later batches in stream order.
+        del xs, temp
+        pending.append([idx, out, offs, sizes, sizes_host, done])
+
+    # Coded tensors are launched in batches of one element size as the list is read (the first
+    # batch smaller), so that the GPU starts while the host reads the rest.
+    cur: dict[tuple[int, bool], tuple[list[int], int]] = {}
+    with contextlib.ExitStack() as ctx:
+        for i, t in enumerate(tensors):
+            if i == 0:  # the scalar arguments once, then each tensor's dtype and rank
+                cd, sub_chunks = _check_args(t, chunk_bytes, sub_chunk_bytes, passthrough_threshold,
+                                             min_compress_bytes, None, pin_memory, compute_device, readback_to_cpu)
+            elif t.dtype not in _CODES:
+                raise TypeError(f"unsupported dtype {t.dtype}")
+            elif t.dim() > _MAX_NDIM:
+                raise ValueError(f"at most {_MAX_NDIM} dimensions are supported")
+            k, n = t.element_size(), t.numel()
+            if n * k < min_compress_bytes or n == 0:
+                small.append(i)
+                continue
+            if device is None:
+                device = _gpu(t.detach(), cd)
+                ctx.enter_context(torch.cuda.device(device))
+                stream = torch.cuda.current_stream(device)
+            key = (k, t.dtype in _REORDER)
+            idx, nbytes = cur.get(key, ([], 0))
+            limit = _DEVICE_BATCH_BYTES if t.is_cuda else _PIPELINE_BYTES
+            if idx and nbytes + n * k > (limit if pending else min(limit, _FIRST_BATCH_BYTES)):
+                launch(key[0], key[1], idx)
+                idx, nbytes = [], 0
+            idx.append(i)
+            cur[key] = (idx, nbytes + n * k)
+        if device is None:
+            if small and not readback_to_cpu:
+                dev = _gpu(tensors[small[0]].detach(), cd)
+                with torch.cuda.device(dev):
+                    compress_small(dev)
+            else:
+                compress_small(None)
+            return blobs  # type: ignore[return-value]
+        for (k, reorder), (idx, _) in cur.items():
+            if idx:
+                launch(k, reorder, idx)
         # The small tensors' host work overlaps the coded kernels.
         compress_small(device)
         if not readback_to_cpu:
             all_sizes = torch.cat([p[3] for p in pending]).cpu().tolist()  # the one synchronization
             pos = 0
             for idx, out, offs, *_ in pending:
-                for i, o in zip(idx, offs):
-                    blobs[i] = out[o : o + all_sizes[pos]]
-                    pos += 1
+                # One split of the batch buffer into (blob, gap) pieces makes every view at once.
+                pieces = []
+                for j, o in enumerate(offs):
+                    size = all_sizes[pos + j]
+                    nxt = offs[j + 1] if j + 1 < len(offs) else out.numel()
+                    pieces += (size, nxt - o - size)
+                views = out.split(pieces)
+                for j, i in enumerate(idx):
+                    blobs[i] = views[2 * j]
+                pos += len(idx)
             return blobs  # type: ignore[return-value]
         copy_out = _side_stream(device, 1)
         for entry in pending:
@@ -731,9 +752,22 @@ def decompress_tensors(
     into one buffer per call (one allocation instead of one per small tensor)."""
     compute_device = _check_device(compute_device)
     outs: list[torch.Tensor | None] = [None] * len(blobs)
-    for blob in blobs:
+    # Headers of GPU blobs come to the host in one copy per device; prefixes[i] = (buffer, offset).
+    plen = [0] * len(blobs)
+    prefixes: list[tuple[memoryview, int] | None] = [None] * len(blobs)
+    by_dev: dict[torch.device, list[int]] = {}
+    for i, blob in enumerate(blobs):
         if blob.dtype != torch.uint8 or blob.dim() != 1:
             raise ValueError("blob must be a 1-D uint8 tensor")
+        plen[i] = p = min(blob.numel(), _FIXED.size + 8 * _MAX_NDIM)
+        if blob.is_cuda:
+            by_dev.setdefault(blob.device, []).append(i)
+        else:
+            prefixes[i] = (memoryview(blob[:p].contiguous().numpy()), 0)
+    for dev, idx in by_dev.items():
+        flat, offs = _gather_prefixes(dev, [blobs[i] for i in idx], [plen[i] for i in idx])
+        for i, o in zip(idx, offs):
+            prefixes[i] = (flat, o)
     small: list[tuple[int, torch.dtype, tuple[int, ...], int]] = []  # stored / empty, after the launches
 
     def decompress_small() -> None:
@@ -774,19 +808,6 @@ def decompress_tensors(
                     pos += (nb + 255) & ~255
             with torch.cuda.device(bdev):
                 _copy_batch(bdev, srcs, dsts, sizes)
-
-    # Headers of GPU blobs come to the host in one copy per device.
-    plen = [min(b.numel(), _FIXED.size + 8 * _MAX_NDIM) for b in blobs]
-    prefixes: list[memoryview | None] = [None] * len(blobs)
-    by_dev: dict[torch.device, list[int]] = {}
-    for i, b in enumerate(blobs):
-        if b.is_cuda:
-            by_dev.setdefault(b.device, []).append(i)
-        else:
-            prefixes[i] = memoryview(b[: plen[i]].contiguous().numpy())
-    for dev, idx in by_dev.items():
-        for i, view in zip(idx, _gather_prefixes(dev, [blobs[i] for i in idx], [plen[i] for i in idx])):
-            prefixes[i] = view
 
     # Coded blobs are launched in batches as they are parsed, so that the GPU starts on the first
     # batch while the host prepares the next.  Host-resident blobs go up on a copy stream in
@@ -845,7 +866,7 @@ def decompress_tensors(
             outs[i] = y
 
     for i, blob in enumerate(blobs):
-        dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefixes[i])
+        dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefixes[i][0], prefixes[i][1], plen[i])
         if flags & _FLAG_STORED or n == 0:
             small.append((i, dtype, shape, flags))
             continue
@@ -891,22 +912,24 @@ def decompress_tensors(
     return outs  # type: ignore[return-value]
 
 
-def _gather_prefixes(device: torch.device, bs: list[torch.Tensor], plen: list[int]) -> list[memoryview]:
-    """The first plen[j] bytes of each device blob, in one device-to-host copy: a batched device
-    copy into one buffer when every blob is 8-byte aligned, else a concatenation."""
+def _gather_prefixes(device: torch.device, bs: list[torch.Tensor], plen: list[int]) -> tuple[memoryview, list[int]]:
+    """The first plen[j] bytes of each device blob, in one device-to-host copy: one host buffer and
+    the offset of each prefix in it.  A batched device copy into one buffer when every blob is
+    8-byte aligned, else a concatenation."""
     with torch.cuda.device(device):
         step = _FIXED.size + 8 * _MAX_NDIM
-        if all(b.data_ptr() % 8 == 0 for b in bs) and all(p > 0 for p in plen):
+        ptrs = [b.data_ptr() for b in bs]
+        if all(p % 8 == 0 for p in ptrs) and all(plen):
             buf = torch.empty(len(bs) * step, dtype=torch.uint8, device=device)
-            _copy_batch(device, [b.data_ptr() for b in bs], [buf.data_ptr() + j * step for j in range(len(bs))], plen)
-            flat = memoryview(buf.cpu().numpy())
-            return [flat[j * step : j * step + p] for j, p in enumerate(plen)]
+            base = buf.data_ptr()
+            _copy_batch(device, ptrs, list(range(base, base + len(bs) * step, step)), plen)
+            return memoryview(buf.cpu().numpy()), list(range(0, len(bs) * step, step))
         flat = memoryview(torch.cat([b[:p] for b, p in zip(bs, plen)]).cpu().numpy())
-        out, pos = [], 0
+        offs, pos = [], 0
         for p in plen:
-            out.append(flat[pos : pos + p])
+            offs.append(pos)
             pos += p
-        return out
+        return flat, offs
 
 
 def _populated_empty(size: int, *, pin_memory: bool = False) -> torch.Tensor:
