@@ -509,55 +509,62 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
 #pragma unroll
       for (int b = 0; b < K; ++b) rp[b] = src[b] + base[0] + l16;
       uint8_t* op = outc + (base[0] + l16) * K;  // 16-byte aligned when outc is (full rounds)
-      for (; r < rfull; ++r) {
-        if (ncoded > 0) {
-          // [ptr, ptr + 16) must be present (synchronous loads only when the ring ran low), then
-          // at most one block is fetched ahead per round, stored at the round's end.
-          const uint32_t need = min((cb.ptr + 16 + 7) & ~7u, end8);
-          while (cb.fill < need) {
-            ring_put(ring[0][0], cb.fill, block(cb.fill / 8));
-            cb.fill += 8;
+      // LAST: the one coded plane is plane K - 1 (the exponent plane of every float type), so the
+      // raw planes and the decoded symbols have fixed places (no per-round plane selection).
+      auto full_rounds = [&](auto last) {
+        constexpr bool LAST = decltype(last)::value;
+        for (; r < rfull; ++r) {
+          if (LAST || ncoded > 0) {
+            // [ptr, ptr + 16) must be present (synchronous loads only when the ring ran low), then
+            // at most one block is fetched ahead per round, stored at the round's end.
+            const uint32_t need = min((cb.ptr + 16 + 7) & ~7u, end8);
+            while (cb.fill < need) {
+              ring_put(ring[0][0], cb.fill, block(cb.fill / 8));
+              cb.fill += 8;
+            }
+            cb.nload = cb.fill < end8 && cb.fill + 8 <= cb.ptr + kRing ? 1u : 0u;
+            if (cb.nload) cb.r0 = block(cb.fill / 8);
           }
-          cb.nload = cb.fill < end8 && cb.fill + 8 <= cb.ptr + kRing ? 1u : 0u;
-          if (cb.nload) cb.r0 = block(cb.fill / 8);
-        }
-        uint32_t p[K][4];
-#pragma unroll
-        for (int b = 0; b < K; ++b)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) p[b][i] = pn[0][b][i];
-        if (r + 1 < rfull) {
-#pragma unroll
-          for (int b = 0; b < K; ++b) {
-            if (coded[b]) continue;
-            const uint2* sp = reinterpret_cast<const uint2*>(rp[b] + kRound);
-            const uint2 v0 = sp[0], v1 = sp[1];
-            pn[0][b][0] = v0.x; pn[0][b][1] = v0.y; pn[0][b][2] = v1.x; pn[0][b][3] = v1.y;
-          }
-        } else if (r + 1 < rounds) {
-          load_raw_round<K, kChains>(src, coded, base, len, r + 1, l, pn);
-        }
-        if (ncoded > 0) {
-          int nact[1] = {kSteps};
-          uint32_t acc[1][4] = {};
-          if (single[0] < 0) decode_round<true>(cur[0], tabs, ring[0], nact, acc);
-          else fill_single(acc, single[0]);
+          uint32_t p[K][4];
 #pragma unroll
           for (int b = 0; b < K; ++b)
-            if (b == pslot[0]) {
 #pragma unroll
-              for (int i = 0; i < 4; ++i) p[b][i] = acc[0][i];
+            for (int i = 0; i < 4; ++i) p[b][i] = pn[0][b][i];
+          if (r + 1 < rfull) {
+#pragma unroll
+            for (int b = 0; b < K; ++b) {
+              if (LAST ? b == K - 1 : coded[b]) continue;
+              const uint2* sp = reinterpret_cast<const uint2*>(rp[b] + kRound);
+              const uint2 v0 = sp[0], v1 = sp[1];
+              pn[0][b][0] = v0.x; pn[0][b][1] = v0.y; pn[0][b][2] = v1.x; pn[0][b][3] = v1.y;
             }
-          if (cb.nload) ring_put(ring[0][0], cb.fill, cb.r0);
-          cb.fill += 8 * cb.nload;
-        }
-        uint32_t e[4 * K];
-        assemble_elements<K, REORDER>(p, e);
-        store_words(op, e, 4 * K, out16);
+          } else if (r + 1 < rounds) {
+            load_raw_round<K, kChains>(src, coded, base, len, r + 1, l, pn);
+          }
+          if (LAST || ncoded > 0) {
+            int nact[1] = {kSteps};
+            uint32_t acc[1][4] = {};
+            if (single[0] < 0) decode_round<true>(cur[0], tabs, ring[0], nact, acc);
+            else fill_single(acc, single[0]);
 #pragma unroll
-        for (int b = 0; b < K; ++b) rp[b] += kRound;
-        op += kRound * K;
-      }
+            for (int b = 0; b < K; ++b)
+              if (LAST ? b == K - 1 : b == pslot[0]) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) p[b][i] = acc[0][i];
+              }
+            if (cb.nload) ring_put(ring[0][0], cb.fill, cb.r0);
+            cb.fill += 8 * cb.nload;
+          }
+          uint32_t e[4 * K];
+          assemble_elements<K, REORDER>(p, e);
+          store_words(op, e, 4 * K, out16);
+#pragma unroll
+          for (int b = 0; b < K; ++b) rp[b] += kRound;
+          op += kRound * K;
+        }
+      };
+      if (ncoded == 1 && pslot[0] == K - 1) full_rounds(std::true_type{});
+      else full_rounds(std::false_type{});
     }
     for (; r < rounds; ++r) {
       int nact[kChains];
