@@ -15,6 +15,7 @@
 //      encoded chunks are still in L2), writes raw planes straight from the elements and copies
 //      the coded payloads from scratch, zero-padding every unit to 8 bytes.
 #include <climits>
+#include <type_traits>
 #include <math.h>
 #include <string.h>
 
@@ -691,30 +692,40 @@ __global__ void __launch_bounds__(kEncThreads, 7) encode_kernel(const EncArgs* _
     if constexpr (kEncChains == 1) {
       const uint8_t* xp = xc + (base[0] + int64_t(r) * kRound + l * kSteps) * K;  // round r's elements
       uint8_t* sp = spec_item ? spec0[0] + int64_t(r) * kRound : nullptr;
-      for (; r >= 0; --r) {
-        uint32_t sym[1][4];
-        plane_of_elements<K, REORDER>(nxt[0], b, sym[0]);
-        if (spec_item) {
+      // LAST: the coded plane is plane K - 1 and every other plane goes to the blob in place, from
+      // 16-byte aligned elements (every float type's usual case): planes and loads fixed at compile
+      // time.
+      auto lean_rounds = [&](auto last) {
+        constexpr bool LAST = decltype(last)::value;
+        for (; r >= 0; --r) {
+          uint32_t sym[1][4];
+          plane_of_elements<K, REORDER>(nxt[0], LAST ? K - 1 : b, sym[0]);
+          if (LAST || spec_item) {
 #pragma unroll
-          for (int q = 0; q < K; ++q) {
-            if (!((spec_mask >> q) & 1)) continue;
-            uint32_t raw[4];
-            plane_of_elements<K, REORDER>(nxt[0], q, raw);
-            uint2* d = reinterpret_cast<uint2*>(sp + q * a.spec_plane_bytes);
-            d[0] = make_uint2(raw[0], raw[1]);
-            d[1] = make_uint2(raw[2], raw[3]);
+            for (int q = 0; q < K; ++q) {
+              if (LAST ? q == K - 1 : !((spec_mask >> q) & 1)) continue;
+              uint32_t raw[4];
+              plane_of_elements<K, REORDER>(nxt[0], q, raw);
+              uint2* d = reinterpret_cast<uint2*>(sp + q * a.spec_plane_bytes);
+              d[0] = make_uint2(raw[0], raw[1]);
+              d[1] = make_uint2(raw[2], raw[3]);
+            }
           }
+          if (r > 0) load_words(xp - kRound * K, nxt[0], 4 * K, LAST || mode == 2);
+          const int nact[1] = {kSteps};
+          encode_round<true>(x, wp, stage, sym, tab, nact);
+          while (flushed[0] - wp[0] >= 8) {
+            flushed[0] -= 8;
+            *reinterpret_cast<uint4*>(out[0] + flushed[0]) = stage_block(stage[0], flushed[0]);
+          }
+          xp -= kRound * K;
+          if (LAST || spec_item) sp -= kRound;
         }
-        if (r > 0) load_words(xp - kRound * K, nxt[0], 4 * K, mode == 2);
-        const int nact[1] = {kSteps};
-        encode_round<true>(x, wp, stage, sym, tab, nact);
-        while (flushed[0] - wp[0] >= 8) {
-          flushed[0] -= 8;
-          *reinterpret_cast<uint4*>(out[0] + flushed[0]) = stage_block(stage[0], flushed[0]);
-        }
-        xp -= kRound * K;
-        if (spec_item) sp -= kRound;
-      }
+      };
+      if (b == K - 1 && spec_mask == (1u << (K - 1)) - 1 && mode == 2 && (K == 1 || spec_item))
+        lean_rounds(std::true_type{});
+      else
+        lean_rounds(std::false_type{});
     }
 #pragma unroll
     for (int c = 0; c < kEncChains; ++c)
