@@ -80,6 +80,7 @@ def test_blobs_equal_reference_container(golden, z):
         ("bfloat16", 200_000, 640, 8192),
         ("int32", 100_000, 4096, 8192),
         ("float64", 50_000, 4096, 8192),
+        ("int16", 300_001, 131072, 8192),
     ],
 )
 def test_gpu_blob_equals_oracle(z, dtype, n, chunk, sub):
@@ -88,6 +89,11 @@ def test_gpu_blob_equals_oracle(z, dtype, n, chunk, sub):
         x = (torch.randn(n, generator=g) * 16).clamp(-448, 448).to(_TORCH[dtype])
     elif dtype == "int32":
         x = torch.randint(-1000, 1000, (n,), generator=g, dtype=torch.int32)
+    elif dtype == "int16":  # skewed low byte (coded), uniform high byte (raw): a coded first plane
+        b = torch.empty(2 * n, dtype=torch.uint8)
+        b[0::2] = (torch.randn(n, generator=g).abs() * 3).clamp(max=255).to(torch.uint8)
+        b[1::2] = torch.randint(0, 256, (n,), generator=g, dtype=torch.uint8)
+        x = b.view(torch.int16)
     else:
         x = (torch.randn(n, generator=g) * 0.02).to(_TORCH[dtype])
     ref = O.compress(_u8(x), x.shape, dtype, chunk_bytes=chunk, sub_chunk_bytes=sub, min_compress_bytes=0,
