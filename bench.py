@@ -328,7 +328,7 @@ def main() -> None:
     coded_bytes = nbytes(coded)
     coded_blob = blob_bytes - (model_bytes - coded_bytes)  # stored blobs add header bytes only
     # Algorithmic bytes per step: the kernel's launches of one step cover all non-stored tensors
-    # (one launch per batch of about 2 GB).
+    # (one launch per batch of about 4 GB).
     algo = {"decode": coded_blob + coded_bytes, "encode": coded_bytes + coded_blob,
             "hist": coded_bytes, "pack": coded_bytes + coded_blob}.get(dominant, coded_bytes)
     peak, peak_src = measured_hbm_peak()

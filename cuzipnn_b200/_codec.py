@@ -478,7 +478,7 @@ def _ptr_array(ctype, values):
 
 
 _PIPELINE_BYTES = 1 << 29  # sub-batch of host-resident inputs (upload overlapped with the kernels)
-_DEVICE_BATCH_BYTES = 1 << 31  # sub-batch of device-resident inputs (launched while the host prepares the next)
+_DEVICE_BATCH_BYTES = 1 << 32  # sub-batch of device-resident inputs (launched while the host prepares the next)
 _FIRST_BATCH_BYTES = 1 << 28  # the first sub-batch of a call is smaller, so that the GPU starts sooner
 _TINY_BYTES = 65536  # stored tensors up to this size decode into views of one shared buffer per call
 _COPY_BATCH_MAX = 1 << 29  # largest single copy of one zn_copy_chunks launch (65535 tiles of 8 KiB)
