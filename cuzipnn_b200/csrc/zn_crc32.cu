@@ -7,9 +7,10 @@
 // zlib returns ~reg with I = 0xFFFFFFFF.  crc0 of a concatenation A|B is crc0(A) * x^(8|B|) xor
 // crc0(B), and leading zero bytes do not change crc0.  So each segment is right-aligned in a
 // virtual block of G equal pieces (zeros in front), every thread computes crc0 of its 128-byte
-// piece with slice-by-8 tables held in shared memory, and a binary tree combines the pieces with
-// the constant multipliers x^(8 * 128 * 2^k).  Segments longer than one block (32 KiB) get one CTA
-// per block and a second kernel combines the block values the same way.
+// piece with slice-by-8 tables held in shared memory, multiplies it by x^(8 * 128 * (pieces after
+// it)) from a precomputed table, and an XOR reduction gives the block's crc0.  Segments longer
+// than one block (32 KiB) get one CTA per block and a second kernel combines the block values with
+// a binary tree of the constant multipliers x^(8 * 32 Ki * 2^k).
 #include "zn_common.cuh"
 
 namespace zn {
@@ -43,6 +44,36 @@ constexpr PowTable make_pow_table() {
 
 __constant__ PowTable c_x8pow = make_pow_table();
 
+// Slice-by-8 tables (T[k][i]: the register after byte i followed by k zero bytes) and the piece
+// multipliers x^(8 * kPiece * m) mod P, m = 0 .. kThreads - 1, computed at compile time.
+struct CrcTables {
+  uint32_t t[8][256];
+  uint32_t piece_pow[256];
+};
+
+constexpr CrcTables make_crc_tables() {
+  CrcTables r{};
+  for (int i = 0; i < 256; ++i) {
+    uint32_t c = uint32_t(i);
+    for (int b = 0; b < 8; ++b) c = (c >> 1) ^ ((c & 1u) ? kPoly : 0u);
+    r.t[0][i] = c;
+  }
+  for (int i = 0; i < 256; ++i) {
+    uint32_t c = r.t[0][i];
+    for (int k = 1; k < 8; ++k) {
+      c = (c >> 8) ^ r.t[0][c & 0xFF];
+      r.t[k][i] = c;
+    }
+  }
+  const uint32_t x_piece = make_pow_table().v[7];  // x^(8 * 128)
+  static_assert(kPiece == 128, "piece_pow assumes 128-byte pieces");
+  r.piece_pow[0] = 0x80000000u;  // x^0
+  for (int m = 1; m < 256; ++m) r.piece_pow[m] = gf2_mul_c(r.piece_pow[m - 1], x_piece);
+  return r;
+}
+
+__device__ const CrcTables g_crc_tables = make_crc_tables();
+
 __device__ __forceinline__ uint32_t gf2_mul(uint32_t a, uint32_t b) {
   uint32_t p = 0;
 #pragma unroll
@@ -65,23 +96,9 @@ __device__ __forceinline__ uint32_t finish(uint32_t crc0, int64_t len) {
   return ~(gf2_mul(0xFFFFFFFFu, x8pow(uint64_t(len))) ^ crc0);
 }
 
-// Slice-by-8 tables: T[k][i] is the register after byte i followed by k zero bytes.
+// Slice-by-8 tables into shared memory, from the precomputed copy.
 __device__ void build_tables(uint32_t (*T)[256]) {
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-    uint32_t c = uint32_t(i);
-#pragma unroll
-    for (int b = 0; b < 8; ++b) c = (c >> 1) ^ (kPoly & (0u - (c & 1u)));
-    T[0][i] = c;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-    uint32_t c = T[0][i];
-#pragma unroll
-    for (int k = 1; k < 8; ++k) {
-      c = (c >> 8) ^ T[0][c & 0xFF];
-      T[k][i] = c;
-    }
-  }
+  for (int i = threadIdx.x; i < 8 * 256; i += blockDim.x) T[i >> 8][i & 255] = g_crc_tables.t[i >> 8][i & 255];
   __syncthreads();
 }
 
@@ -138,8 +155,7 @@ __global__ void __launch_bounds__(kThreads) crc_level1(const uint8_t* __restrict
                                                        int64_t nseg, int G, int64_t blocks_per_seg, bool single_level,
                                                        uint32_t* __restrict__ out, uint32_t* __restrict__ partial) {
   __shared__ uint32_t T[8][256];
-  __shared__ uint32_t sm[kThreads];
-  __shared__ uint32_t mult[16];
+  __shared__ uint32_t sm[kThreads / 32];
   build_tables(T);
   const int t = threadIdx.x;
   int64_t s, b;
@@ -165,7 +181,18 @@ __global__ void __launch_bounds__(kThreads) crc_level1(const uint8_t* __restrict
     const int64_t lo = max(v0 - pad, int64_t(0)), hi = min(v0 + kPiece - pad, L);
     if (hi > lo) c = crc_piece(data + s * seg, lo, hi, T);
   }
-  c = combine_group(c, G, kPiece, sm, mult);
+  // The group's crc0 is the XOR over its pieces of crc0 * x^(8 * kPiece * (pieces after it)):
+  // one multiplication per thread by a precomputed power, then an XOR reduction.
+  if (c) c = gf2_mul(c, g_crc_tables.piece_pow[G - 1 - lt]);
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1)
+    if (o < G) c ^= __shfl_xor_sync(0xFFFFFFFFu, c, o);
+  if (G > 32) {  // groups of whole warps: XOR the warps' values
+    if ((t & 31) == 0) sm[t >> 5] = c;
+    __syncthreads();
+    if (lt == 0)
+      for (int w = 1; w < G / 32; ++w) c ^= sm[(t >> 5) + w];
+  }
   if (lt == 0 && s < nseg) {
     if (single_level) out[s] = finish(c, L);
     else partial[s * blocks_per_seg + b] = c;
