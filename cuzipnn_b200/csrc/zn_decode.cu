@@ -279,6 +279,43 @@ __device__ __forceinline__ void decode_round(Cursor* cb, const uint32_t* __restr
   }
 }
 
+// The fast path's 16 steps of the lane's kChains states.  A state's ring position is kept as the
+// byte offset tid * 4 + (ptr % kRing) * kDecThreads * 4 from its ring's first row, so the word
+// read after a renormalisation costs one masked add; the position advance is recovered at the end
+// (a round consumes at most 16 < kRing words).
+__device__ __forceinline__ void decode_round_fast(Cursor* cb, const uint32_t* __restrict__ tab, const uint8_t* rows,
+                                                  int tid, uint32_t (*acc)[4]) {
+  constexpr uint32_t kRowBytes = kDecThreads * 4, kRingBytes = kRing * kRowBytes;
+  uint32_t xv[kChains], ro[kChains], ro0[kChains], wn[kChains];
+#pragma unroll
+  for (int c = 0; c < kChains; ++c) {
+    xv[c] = cb[c].x;
+    ro0[c] = uint32_t(tid) * 4 + (cb[c].ptr & (kRing - 1)) * kRowBytes;
+    ro[c] = ro0[c];
+    wn[c] = *reinterpret_cast<const uint32_t*>(rows + c * kRingBytes + ro[c]);
+  }
+#define ZN_FSTEP(I)                                                                                   \
+  _Pragma("unroll") for (int c = 0; c < kChains; ++c) {                                               \
+    const uint32_t e = tab[xv[c] & (kM - 1)];                                                         \
+    const uint32_t xn = (e >> 20) * (xv[c] >> kScaleBits) + (e & 0xFFFu);                             \
+    acc[c][(I) >> 2] = __byte_perm(acc[c][(I) >> 2], e >> 12,                                         \
+                                   (0x3210 & ~(0xF << (4 * ((I) & 3)))) | (4 << (4 * ((I) & 3))));    \
+    const bool need = xn < kL;                                                                        \
+    const uint32_t w = wn[c];                                                                         \
+    ro[c] = need ? ((ro[c] + kRowBytes) & (kRingBytes - 1)) : ro[c];                                  \
+    wn[c] = *reinterpret_cast<const uint32_t*>(rows + c * kRingBytes + ro[c]);                        \
+    xv[c] = need ? __byte_perm(w, xn, 0x5410) : xn;                                                   \
+  }
+  ZN_FSTEP(0) ZN_FSTEP(1) ZN_FSTEP(2) ZN_FSTEP(3) ZN_FSTEP(4) ZN_FSTEP(5) ZN_FSTEP(6) ZN_FSTEP(7)
+  ZN_FSTEP(8) ZN_FSTEP(9) ZN_FSTEP(10) ZN_FSTEP(11) ZN_FSTEP(12) ZN_FSTEP(13) ZN_FSTEP(14) ZN_FSTEP(15)
+#undef ZN_FSTEP
+#pragma unroll
+  for (int c = 0; c < kChains; ++c) {
+    cb[c].x = xv[c];
+    cb[c].ptr += (ro[c] / kRowBytes - ro0[c] / kRowBytes) & (kRing - 1);
+  }
+}
+
 // The 16 symbols of a round of a one-symbol plane, for every chain.
 __device__ __forceinline__ void fill_single(uint32_t (*acc)[4], int s) {
 #pragma unroll
@@ -489,14 +526,19 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
     uint32_t pn[kChains][K][4];
     load_raw_round<K, kChains>(src, coded, base, len, 0, l, pn);
     int r = 0;
-    if constexpr (KC == 1 && kChains == 1) {
-      // Full rounds (all 16 steps of this lane's state valid): no per-step predication, 32-bit
-      // bookkeeping and running raw / output pointers; the partial rounds at the end of a
-      // sub-chunk take the general loop below.
+    if constexpr (KC == 1) {
+      // Full rounds (all 16 steps of every chain's state valid): no per-step predication, 32-bit
+      // bookkeeping and running element offsets; the partial rounds at the end of a sub-chunk
+      // take the general loop below.
       const int64_t l16 = int64_t(l) * kSteps;
-      const int rfull = len[0] >= l16 + kSteps ? int((len[0] - l16 - kSteps) / kRound) + 1 : 0;
-      Cursor& cb = cur[0][0];
-      const uint32_t end8 = (cb.end + 7) & ~7u;
+      int rfull = rounds;
+      uint32_t end8[kChains], off[kChains];  // off: element offset of the lane's round r in the chunk
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) {
+        rfull = min(rfull, len[c] >= l16 + kSteps ? int((len[c] - l16 - kSteps) / kRound) + 1 : 0);
+        end8[c] = (cur[0][c].end + 7) & ~7u;
+        off[c] = uint32_t(base[c] + l16);
+      }
       // Stream blocks [qbeg, qend) from gb lie wholly inside [lo, hi): one 16-byte load each.
       const uint4* gb4 = reinterpret_cast<const uint4*>(gb[0]);
       const uint32_t qbeg = gb[0] < lo[0] ? 1u : 0u;
@@ -505,10 +547,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
       auto block = [&](uint32_t q) {
         return q >= qbeg && q < qend ? __ldg(gb4 + q) : load_block(gb[0], q, lo[0], hi[0]);
       };
-      const uint8_t* rp[K];
-#pragma unroll
-      for (int b = 0; b < K; ++b) rp[b] = src[b] + base[0] + l16;
-      uint8_t* op = outc + (base[0] + l16) * K;  // 16-byte aligned when outc is (full rounds)
+      const uint8_t* rows = reinterpret_cast<const uint8_t*>(rings);
       // LAST: the one coded plane is plane K - 1 (the exponent plane of every float type), so the
       // raw planes and the decoded symbols have fixed places (no per-round plane selection).
       auto full_rounds = [&](auto last) {
@@ -517,50 +556,62 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
           if (LAST || ncoded > 0) {
             // [ptr, ptr + 16) must be present (synchronous loads only when the ring ran low), then
             // at most one block is fetched ahead per round, stored at the round's end.
-            const uint32_t need = min((cb.ptr + 16 + 7) & ~7u, end8);
-            while (cb.fill < need) {
-              ring_put(ring[0][0], cb.fill, block(cb.fill / 8));
-              cb.fill += 8;
+#pragma unroll
+            for (int c = 0; c < kChains; ++c) {
+              Cursor& cb = cur[0][c];
+              const uint32_t need = min((cb.ptr + 16 + 7) & ~7u, end8[c]);
+              while (cb.fill < need) {
+                ring_put(ring[0][c], cb.fill, block(cb.fill / 8));
+                cb.fill += 8;
+              }
+              cb.nload = cb.fill < end8[c] && cb.fill + 8 <= cb.ptr + kRing ? 1u : 0u;
+              if (cb.nload) cb.r0 = block(cb.fill / 8);
             }
-            cb.nload = cb.fill < end8 && cb.fill + 8 <= cb.ptr + kRing ? 1u : 0u;
-            if (cb.nload) cb.r0 = block(cb.fill / 8);
           }
-          uint32_t p[K][4];
+          uint32_t p[kChains][K][4];
 #pragma unroll
-          for (int b = 0; b < K; ++b)
+          for (int c = 0; c < kChains; ++c)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) p[b][i] = pn[0][b][i];
+            for (int b = 0; b < K; ++b)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) p[c][b][i] = pn[c][b][i];
           if (r + 1 < rfull) {
 #pragma unroll
-            for (int b = 0; b < K; ++b) {
-              if (LAST ? b == K - 1 : coded[b]) continue;
-              const uint2* sp = reinterpret_cast<const uint2*>(rp[b] + kRound);
-              const uint2 v0 = sp[0], v1 = sp[1];
-              pn[0][b][0] = v0.x; pn[0][b][1] = v0.y; pn[0][b][2] = v1.x; pn[0][b][3] = v1.y;
-            }
+            for (int c = 0; c < kChains; ++c)
+#pragma unroll
+              for (int b = 0; b < K; ++b) {
+                if (LAST ? b == K - 1 : coded[b]) continue;
+                const uint2* sp = reinterpret_cast<const uint2*>(src[b] + off[c] + kRound);
+                const uint2 v0 = sp[0], v1 = sp[1];
+                pn[c][b][0] = v0.x; pn[c][b][1] = v0.y; pn[c][b][2] = v1.x; pn[c][b][3] = v1.y;
+              }
           } else if (r + 1 < rounds) {
             load_raw_round<K, kChains>(src, coded, base, len, r + 1, l, pn);
           }
           if (LAST || ncoded > 0) {
-            int nact[1] = {kSteps};
-            uint32_t acc[1][4] = {};
-            if (single[0] < 0) decode_round<true>(cur[0], tabs, ring[0], nact, acc);
+            uint32_t acc[kChains][4] = {};
+            if (single[0] < 0) decode_round_fast(cur[0], tabs, rows, tid, acc);
             else fill_single(acc, single[0]);
 #pragma unroll
-            for (int b = 0; b < K; ++b)
-              if (LAST ? b == K - 1 : b == pslot[0]) {
+            for (int c = 0; c < kChains; ++c) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) p[b][i] = acc[0][i];
-              }
-            if (cb.nload) ring_put(ring[0][0], cb.fill, cb.r0);
-            cb.fill += 8 * cb.nload;
+              for (int b = 0; b < K; ++b)
+                if (LAST ? b == K - 1 : b == pslot[0]) {
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) p[c][b][i] = acc[c][i];
+                }
+              Cursor& cb = cur[0][c];
+              if (cb.nload) ring_put(ring[0][c], cb.fill, cb.r0);
+              cb.fill += 8 * cb.nload;
+            }
           }
-          uint32_t e[4 * K];
-          assemble_elements<K, REORDER>(p, e);
-          store_words(op, e, 4 * K, out16);
 #pragma unroll
-          for (int b = 0; b < K; ++b) rp[b] += kRound;
-          op += kRound * K;
+          for (int c = 0; c < kChains; ++c) {
+            uint32_t e[4 * K];
+            assemble_elements<K, REORDER>(p[c], e);
+            store_words(outc + size_t(off[c]) * K, e, 4 * K, out16);  // 16-byte aligned when outc is
+            off[c] += kRound;
+          }
         }
       };
       if (ncoded == 1 && pslot[0] == K - 1) full_rounds(std::true_type{});

@@ -398,6 +398,31 @@ __device__ __forceinline__ void encode_round(uint32_t* x, uint32_t* wp, uint32_t
 #undef ZN_ESTEP
 }
 
+// The lean loop's 16 steps.  The staging position is kept as the byte offset
+// tid * 4 + (wp % 32) * kEncThreads * 4 into the rows of the staging ring, so an emission costs
+// one masked subtract and one store; wp is recovered at the end (a round emits at most 16 < 32
+// words).
+__device__ __forceinline__ void encode_round_lean(uint32_t& x, uint32_t& wp, uint8_t* rows, int tid,
+                                                  const uint32_t* sym, const uint4* tab) {
+  constexpr uint32_t kRowBytes = kEncThreads * 4, kRingBytes = 32 * kRowBytes;
+  const uint32_t wo0 = uint32_t(tid) * 4 + (wp & 31) * kRowBytes;
+  uint32_t wo = wo0;
+#define ZN_LSTEP(I)                                                                               \
+  {                                                                                               \
+    const uint4 e = tab[get_byte(sym, I)];                                                        \
+    const bool emit = x > e.w;                                                                    \
+    wo = emit ? ((wo - kRowBytes) & (kRingBytes - 1)) : wo;                                       \
+    if (emit) *reinterpret_cast<uint32_t*>(rows + wo) = x;                                        \
+    x = emit ? x >> 16 : x;                                                                       \
+    const uint32_t q = __funnelshift_r(__umulhi(x, e.x), 0u, e.z);                                \
+    x = x + e.y + q * (e.z >> 5);                                                                 \
+  }
+  ZN_LSTEP(15) ZN_LSTEP(14) ZN_LSTEP(13) ZN_LSTEP(12) ZN_LSTEP(11) ZN_LSTEP(10) ZN_LSTEP(9) ZN_LSTEP(8)
+  ZN_LSTEP(7) ZN_LSTEP(6) ZN_LSTEP(5) ZN_LSTEP(4) ZN_LSTEP(3) ZN_LSTEP(2) ZN_LSTEP(1) ZN_LSTEP(0)
+#undef ZN_LSTEP
+  wp -= (wo0 / kRowBytes - wo / kRowBytes) & 31u;
+}
+
 // ---- the encoder ----------------------------------------------------------------------------
 
 template <int K, bool REORDER>
@@ -712,8 +737,7 @@ __global__ void __launch_bounds__(kEncThreads, 7) encode_kernel(const EncArgs* _
             }
           }
           if (r > 0) load_words(xp - kRound * K, nxt[0], 4 * K, LAST || mode == 2);
-          const int nact[1] = {kSteps};
-          encode_round<true>(x, wp, stage, sym, tab, nact);
+          encode_round_lean(x[0], wp[0], reinterpret_cast<uint8_t*>(&S.stage[0][0]), tid, sym[0], tab);
           while (flushed[0] - wp[0] >= 8) {
             flushed[0] -= 8;
             *reinterpret_cast<uint4*>(out[0] + flushed[0]) = stage_block(stage[0], flushed[0]);
@@ -1036,7 +1060,7 @@ template <int K>
 constexpr int kPackGroups = K >= 4 ? 1 : 4 / K;
 
 template <int K, bool REORDER>
-__global__ void __launch_bounds__(kPackThreads, 4) pack_kernel(const EncArgs* __restrict__ jobs, int njobs, int64_t total_chunks) {
+__global__ void __launch_bounds__(kPackThreads, 5) pack_kernel(const EncArgs* __restrict__ jobs, int njobs, int64_t total_chunks) {
   __shared__ PayloadSmem P;
   const int64_t gj = total_chunks - 1 - blockIdx.x / kPackParts;
   const EncArgs& a = jobs[find_job(jobs, njobs, gj)];
