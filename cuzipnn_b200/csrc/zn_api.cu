@@ -41,7 +41,17 @@ int set_max_smem(const void* func, int bytes) {
   if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("cudaGetDevice");
   std::lock_guard<std::mutex> lock(mu);
   if (bytes <= 48 * 1024 || done.count({func, dev})) return ZN_OK;
-  cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  // The opt-in limit covers static and dynamic shared memory together.
+  cudaFuncAttributes fa{};
+  int optin = 0;
+  cudaError_t e = cudaFuncGetAttributes(&fa, func);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e == cudaSuccess) {
+    if (bytes > optin - int(fa.sharedSizeBytes))
+      return set_error(ZN_ERR_CUDA, "kernel needs %d bytes of shared memory, the device allows %d", bytes,
+                       optin - int(fa.sharedSizeBytes));
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - int(fa.sharedSizeBytes));
+  }
   if (e != cudaSuccess) return set_error(ZN_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   done.insert({func, dev});
   return ZN_OK;

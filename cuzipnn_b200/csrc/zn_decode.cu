@@ -375,20 +375,22 @@ __device__ __forceinline__ void assemble_elements(const uint32_t (*p)[4], uint32
   }
 }
 
-// KC: coded planes per chunk held in shared memory.  The main pass (KC = 1 for K > 1) flags
-// chunks with more coded planes; a second pass with KC = K decodes only those.
+// Decode global chunk gchunk with the whole CTA.  KC: coded planes per chunk held in shared
+// memory.  The main pass (KC = 1 for K > 1) flags chunks with more coded planes; a second pass
+// with KC = K decodes only those.  Every return is taken by all threads of the CTA together.
 // Work split: a warp item is 8 sub-chunks; lane l of 8-lane segment g runs chain c on sub-chunk
 // 8 * item + 4 * c + g.
 template <int K, bool REORDER, int KC>
-__global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __restrict__ jobs, int njobs, bool overflow_pass) {
+__device__ __forceinline__ void decode_chunk(const DecArgs* __restrict__ jobs, int njobs, int64_t gchunk,
+                                             bool overflow_pass) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   using Slot = RingSlot<KC>;
   uint32_t* tabs = reinterpret_cast<uint32_t*>(smem_raw);                      // [KC][4096]
   Slot* rings = reinterpret_cast<Slot*>(smem_raw + KC * kM * 4);                // [KC][kChains][kRing][threads]
   DecSmem& S = *reinterpret_cast<DecSmem*>(smem_raw + KC * kM * 4 + KC * kChains * kRing * kDecThreads * sizeof(Slot));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const DecArgs& a = jobs[find_job(jobs, njobs, blockIdx.x)];
-  const int64_t j = blockIdx.x - a.chunk0;
+  const DecArgs& a = jobs[find_job(jobs, njobs, gchunk)];
+  const int64_t j = gchunk - a.chunk0;
   if (overflow_pass && !a.overflow[j]) return;
   const bool batched = a.in_ptrs != nullptr;
   int64_t m;
@@ -714,6 +716,41 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __re
   }
 }
 
+// Main pass: one CTA per chunk.
+template <int K, bool REORDER, int KC>
+__global__ void __launch_bounds__(kDecThreads) decode_kernel(const DecArgs* __restrict__ jobs, int njobs) {
+  decode_chunk<K, REORDER, KC>(jobs, njobs, blockIdx.x, false);
+}
+
+// Overflow pass: a grid of resident CTAs scans the per-chunk flags, kDecThreads chunks a round at a
+// stride of the grid (flagged chunks that cluster in one tensor spread over the CTAs), and decodes
+// the flagged ones one after another.
+template <int K, bool REORDER, int KC>
+__global__ void __launch_bounds__(kDecThreads) decode_overflow_kernel(const DecArgs* __restrict__ jobs, int njobs,
+                                                                      int64_t total_chunks) {
+  __shared__ int64_t flagged[kDecThreads];
+  __shared__ int nflagged;
+  const int64_t stride = gridDim.x;
+  for (int64_t first = blockIdx.x; first < total_chunks; first += stride * kDecThreads) {
+    const int64_t c = first + stride * threadIdx.x;
+    bool f = false;
+    if (c < total_chunks) {
+      const DecArgs& a = jobs[find_job(jobs, njobs, c)];
+      f = a.overflow[c - a.chunk0] != 0;
+    }
+    if (threadIdx.x == 0) nflagged = 0;
+    __syncthreads();
+    if (f) flagged[atomicAdd(&nflagged, 1)] = c;
+    __syncthreads();
+    const int nf = nflagged;
+    for (int q = 0; q < nf; ++q) {
+      decode_chunk<K, REORDER, KC>(jobs, njobs, flagged[q], true);
+      __syncthreads();
+    }
+    __syncthreads();
+  }
+}
+
 // ---- table scan (src/cuzipnn/_codec.py:492-496, 529) ----------------------------------------
 
 constexpr int kScanThreads = 1024;
@@ -782,14 +819,25 @@ size_t dec_smem(int KC) {
   return size_t(KC) * kM * 4 + size_t(KC) * kChains * kRing * kDecThreads * (KC > 4 ? 2 : 4) + sizeof(DecSmem);
 }
 
-template <int K, bool REORDER, int KC>
-int launch_decode_pass(const DecArgs* jobs, int njobs, int64_t grid, bool overflow_pass, cudaStream_t s) {
+template <int K, bool REORDER, int KC, bool OVERFLOW>
+int launch_decode_pass(const DecArgs* jobs, int njobs, int64_t total_chunks, cudaStream_t s) {
   const size_t sm = dec_smem(KC);
-  auto fn = decode_kernel<K, REORDER, KC>;
-  if (int rc = set_max_smem(reinterpret_cast<const void*>(fn), int(sm))) return rc;
-  {
-    TimedLaunch tl(overflow_pass ? "decode_overflow" : "decode", s);
-    fn<<<unsigned(grid), kDecThreads, sm, s>>>(jobs, njobs, overflow_pass);
+  if constexpr (!OVERFLOW) {
+    auto fn = decode_kernel<K, REORDER, KC>;
+    if (int rc = set_max_smem(reinterpret_cast<const void*>(fn), int(sm))) return rc;
+    TimedLaunch tl("decode", s);
+    fn<<<unsigned(total_chunks), kDecThreads, sm, s>>>(jobs, njobs);
+  } else {
+    auto fn = decode_overflow_kernel<K, REORDER, KC>;
+    if (int rc = set_max_smem(reinterpret_cast<const void*>(fn), int(sm))) return rc;
+    int dev = 0, sms = 0, per_sm = 0;  // the grid: the CTAs that fit on the device at once
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kDecThreads, sm);
+    if (e != cudaSuccess) return set_error(ZN_ERR_CUDA, "decode_overflow_kernel occupancy: %s", cudaGetErrorString(e));
+    const int64_t grid = min(total_chunks, int64_t(max(1, sms * per_sm)));
+    TimedLaunch tl("decode_overflow", s);
+    fn<<<unsigned(grid), kDecThreads, sm, s>>>(jobs, njobs, total_chunks);
   }
   count_launch();
   return check_launch("decode_kernel");
@@ -799,8 +847,8 @@ int launch_decode_pass(const DecArgs* jobs, int njobs, int64_t grid, bool overfl
 template <int K, bool REORDER>
 int launch_decode(const DecArgs* jobs, int njobs, int64_t grid, cudaStream_t s) {
   if (grid <= 0) return ZN_OK;
-  if (int rc = launch_decode_pass<K, REORDER, 1>(jobs, njobs, grid, false, s)) return rc;
-  if constexpr (K > 1) return launch_decode_pass<K, REORDER, K>(jobs, njobs, grid, true, s);
+  if (int rc = launch_decode_pass<K, REORDER, 1, false>(jobs, njobs, grid, s)) return rc;
+  if constexpr (K > 1) return launch_decode_pass<K, REORDER, K, true>(jobs, njobs, grid, s);
   return ZN_OK;
 }
 
