@@ -106,6 +106,24 @@ def test_gpu_blob_equals_oracle(z, dtype, n, chunk, sub):
     assert np.array_equal(_u8(y), _u8(x))
 
 
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32", "float64"])
+def test_overflow_pass_many_chunks(z, dtype):
+    """Every chunk has several coded planes (16 distinct values: the low mantissa planes hold one
+    symbol each), so every chunk goes to the overflow pass, whose CTAs (as many as fit on the GPU)
+    decode several chunks each."""
+    g = torch.Generator().manual_seed(5)
+    n = 1 << 21
+    x = (torch.randint(0, 16, (n,), generator=g).double() * 0.125).to(_TORCH[dtype])
+    ref = O.compress(_u8(x), x.shape, dtype, chunk_bytes=2048, sub_chunk_bytes=2048, min_compress_bytes=0,
+                     threads=8)
+    blob = z.compress_tensor(x.cuda(), chunk_bytes=2048, sub_chunk_bytes=2048, min_compress_bytes=0)
+    assert np.array_equal(_u8(blob), np.frombuffer(ref, dtype=np.uint8))
+    y = z.decompress_tensor(blob)
+    torch.cuda.synchronize()
+    assert z.last_decode_status() == 0
+    assert np.array_equal(_u8(y), _u8(x))
+
+
 def test_split_matches_reference(golden):
     from cuzipnn_b200 import _kernels
 
