@@ -256,9 +256,8 @@ int set_max_smem(const void* func, int bytes);
 
 // Copy `count` host structs to device memory at dev, on stream s, through kernel parameters, and
 // (for more than one job) build the chunk -> job map behind them (job_table_bytes).
-template <class T>
-int upload_jobs(const T* host, int count, T* dev, int64_t total_chunks, cudaStream_t s) {
-  constexpr int N = 30000 / int(sizeof(T)) > 0 ? 30000 / int(sizeof(T)) : 1;
+template <class T, int N>
+int upload_batches(const T* host, int count, T* dev, cudaStream_t s) {
   for (int i = 0; i < count; i += N) {
     UploadBatch<T, N> b;
     b.count = count - i < N ? count - i : N;
@@ -267,6 +266,16 @@ int upload_jobs(const T* host, int count, T* dev, int64_t total_chunks, cudaStre
     count_launch();
     if (int rc = check_launch("upload_kernel")) return rc;
   }
+  return ZN_OK;
+}
+
+template <class T>
+int upload_jobs(const T* host, int count, T* dev, int64_t total_chunks, cudaStream_t s) {
+  // Batches of up to ~30 KB of kernel parameters; a call with a few jobs (one tensor) takes a
+  // small parameter block instead, since the launch cost grows with the block's size.
+  constexpr int N = 30000 / int(sizeof(T)) > 0 ? 30000 / int(sizeof(T)) : 1;
+  const int rc = count <= 4 ? upload_batches<T, 4>(host, count, dev, s) : upload_batches<T, N>(host, count, dev, s);
+  if (rc) return rc;
   if (count > 1 && total_chunks > 0) {
     map_jobs_kernel<T><<<unsigned(count), 256, 0, s>>>(dev, count, total_chunks);
     count_launch();
