@@ -32,6 +32,7 @@ import contextlib
 import ctypes
 import math
 import struct
+import threading
 import zlib
 from collections.abc import Buffer
 
@@ -368,19 +369,26 @@ def _parse_header(prefix: Buffer, off: int = 0, length: int | None = None
     return _DTYPES[code], shape, flags, chunk_bytes, n_comp, n
 
 
-# Status word of the latest decompress_tensor call per device (0 = no decoding error).
-_LAST_STATUS: dict[int, torch.Tensor] = {}
+# Status words of the calling thread's latest decompress call per device (0 = no decoding error).
+# Per thread, so that threads decoding on one device do not overwrite each other's status.
+_STATUS = threading.local()
+
+
+def _set_status(device: torch.device, status: torch.Tensor) -> None:
+    if not hasattr(_STATUS, "by_dev"):
+        _STATUS.by_dev = {}
+    _STATUS.by_dev[device.index] = status
 
 
 def last_decode_status(device: torch.device | str | int | None = None) -> int:
-    """Error bits the device kernels reported for the latest decompress_tensor on `device`
-    (synchronizes with it).  0 means every unit decoded and validated; nonzero means the blob was
-    malformed (the affected elements were zeroed).  decompress_tensor checks this itself when it
-    synchronizes anyway (readback_to_cpu=True)."""
+    """Error bits the device kernels reported for this thread's latest decompress_tensor (or
+    decompress_tensors) call on `device` (synchronizes with it).  0 means every unit decoded and
+    validated; nonzero means the blob was malformed (the affected elements were zeroed).
+    decompress_tensor checks this itself when it synchronizes anyway (readback_to_cpu=True)."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     if dev.type == "cuda" and dev.index is None:
         dev = torch.device("cuda", torch.cuda.current_device())
-    st = _LAST_STATUS.get(dev.index if dev.type == "cuda" else int(dev))
+    st = getattr(_STATUS, "by_dev", {}).get(dev.index if dev.type == "cuda" else int(dev))
     if st is None:
         return 0
     bits = 0
@@ -389,13 +397,35 @@ def last_decode_status(device: torch.device | str | int | None = None) -> int:
     return bits
 
 
+def _check_out(out: torch.Tensor, dtype: torch.dtype, shape: tuple[int, ...], cpu: bool) -> None:
+    """A caller's output tensor must match the blob's tensor: same dtype (TypeError otherwise), same
+    shape, contiguous, and on the CPU (readback_to_cpu) or a GPU (ValueError otherwise)."""
+    if out.dtype != dtype:
+        raise TypeError(f"out has dtype {out.dtype}, the blob holds {dtype}")
+    if tuple(out.shape) != tuple(shape):
+        raise ValueError(f"out has shape {tuple(out.shape)}, the blob holds {tuple(shape)}")
+    if not out.is_contiguous():
+        raise ValueError("out must be contiguous")
+    if cpu and out.is_cuda:
+        raise ValueError("out must be a CPU tensor with readback_to_cpu")
+    if not cpu and not out.is_cuda:
+        raise ValueError("out must be a CUDA tensor without readback_to_cpu")
+
+
 def decompress_tensor(
     blob: torch.Tensor,
     *,
     compute_device: torch.device | str | None = None,
     readback_to_cpu: bool = False,
+    out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Decompress a blob produced by compress_tensor; the blob may be on the CPU or the GPU.
+
+    With `out` (an addition to the reference's signature, whose call allocates its result each
+    time), the tensor is decoded straight into the caller's storage and `out` is returned: a
+    contiguous tensor of the blob's dtype and shape, on a GPU (it sets the compute device, which
+    compute_device must then name too) or, with readback_to_cpu, on the CPU.  A loader can so fill
+    pre-allocated weights without an extra copy or allocation.
 
     Passing a blob that is not from `compress_tensor` gives an unspecified result (never an
     out-of-bounds access); last_decode_status() reports it.
@@ -410,6 +440,12 @@ def decompress_tensor(
     prefix = (ctypes.c_byte * prefix_len).from_address(prefix_tensor.data_ptr())
     dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefix)
     reorder = bool(flags & _FLAG_REORDER)
+    if out is not None:
+        _check_out(out, dtype, shape, readback_to_cpu)
+        if out.is_cuda:
+            if compute_device is not None and _gpu(blob, compute_device) != out.device:
+                raise ValueError("out is not on compute_device")
+            compute_device = out.device
 
     if flags & _FLAG_STORED:
         # Stored uncompressed: copy the bytes after the header straight to the target device.
@@ -417,23 +453,27 @@ def decompress_tensor(
         nbytes = math.prod(shape) * dtype.itemsize
         if blob.numel() < header_size + nbytes:
             raise ValueError("blob is truncated")
-        if readback_to_cpu:
-            out = _populated_empty(nbytes).view(dtype).view(shape)
-        else:
-            out = torch.empty(shape, dtype=dtype, device=_gpu(blob, compute_device))
+        if out is None:
+            if readback_to_cpu:
+                out = _populated_empty(nbytes).view(dtype).view(shape)
+            else:
+                out = torch.empty(shape, dtype=dtype, device=_gpu(blob, compute_device))
         out.view(-1).view(torch.uint8).copy_(blob[header_size : header_size + nbytes])
         return out
 
     if n == 0:
+        if out is not None:
+            return out
         return torch.empty(
             shape, dtype=dtype, device="cpu" if readback_to_cpu else _gpu(blob, compute_device)
         )
     if math.prod(shape) != n or chunk_bytes <= 0:
         raise ValueError("not a cuzipnn blob")
     device = _gpu(blob, compute_device)
-    out = torch.empty(shape, dtype=dtype, device=device)
+    host_out = out if readback_to_cpu else None
+    y = out if (out is not None and not readback_to_cpu) else torch.empty(shape, dtype=dtype, device=device)
 
-    k = out.element_size()
+    k = y.element_size()
     nch = -(-n // chunk_bytes)
     total = k * nch
     _, _, data_off = _layout(len(shape), total, n_comp)
@@ -454,23 +494,24 @@ def decompress_tensor(
         _lib.check(
             _lib.lib.zn_decompress(
                 x.data_ptr(), x.numel(), n, k, int(reorder), len(shape), chunk_bytes, n_comp,
-                out.data_ptr(), status.data_ptr(), temp.data_ptr(), temp_bytes, _stream(device),
+                y.data_ptr(), status.data_ptr(), temp.data_ptr(), temp_bytes, _stream(device),
             ),
             "zn_decompress",
         )
-        _LAST_STATUS[device.index] = status
+        _set_status(device, status)
 
         if uploaded is not None:
             uploaded.synchronize()
 
         if readback_to_cpu:
-            src = out
-            out = _populated_empty(src.numel() * src.element_size()).view(src.dtype).view_as(src)
-            out.copy_(src)
+            src = y
+            y = host_out if host_out is not None else (
+                _populated_empty(src.numel() * src.element_size()).view(src.dtype).view_as(src))
+            y.copy_(src)
             if int(status.item()):
                 raise ValueError(f"blob is corrupt (decoder status {int(status.item())})")
 
-        return out
+        return y
 
 
 def _ptr_array(ctype, values):
@@ -744,13 +785,21 @@ def decompress_tensors(
     *,
     compute_device: torch.device | str | None = None,
     readback_to_cpu: bool = False,
+    out: list[torch.Tensor | None] | None = None,
 ) -> list[torch.Tensor]:
     """decompress_tensor over a list of blobs, with one kernel launch per stage for each batch of
     blobs of an element size (batches of about _DEVICE_BATCH_BYTES, or _PIPELINE_BYTES for host
     blobs, launched while the host prepares the next).  Decoding errors are reported by
     last_decode_status().  Stored-path tensors of up to _TINY_BYTES decoded on the GPU are views
-    into one buffer per call (one allocation instead of one per small tensor)."""
+    into one buffer per call (one allocation instead of one per small tensor).
+
+    `out`, if given, has one entry per blob: None (allocate, as above) or the caller's tensor to
+    decode into, with decompress_tensor's rules for `out` (on the call's compute device without
+    readback_to_cpu); the returned list then holds those tensors."""
     compute_device = _check_device(compute_device)
+    if out is not None and len(out) != len(blobs):
+        raise ValueError("out must have one entry per blob")
+    dest = list(out) if out is not None else [None] * len(blobs)
     outs: list[torch.Tensor | None] = [None] * len(blobs)
     # Headers of GPU blobs come to the host in one copy per device; prefixes[i] = (buffer, offset).
     plen = [0] * len(blobs)
@@ -782,21 +831,23 @@ def decompress_tensors(
             if (flags & _FLAG_STORED and b.is_cuda and not readback_to_cpu and 0 < nbytes <= _COPY_BATCH_MAX
                     and (b.data_ptr() + header_size) % 8 == 0
                     and (compute_device is None or _gpu(b, compute_device) == b.device)
+                    and (dest[i] is None or (dest[i].device == b.device and dest[i].data_ptr() % 8 == 0))
                     and bdev in (None, b.device)):
                 bdev = b.device
                 if b.numel() < header_size + nbytes:
                     raise ValueError("blob is truncated")
                 srcs.append(b.data_ptr() + header_size)
                 sizes.append(nbytes)
-                if nbytes <= _TINY_BYTES:  # placed in one shared buffer below
+                if dest[i] is None and nbytes <= _TINY_BYTES:  # placed in one shared buffer below
                     tiny.append((i, dtype, shape, nbytes, len(dsts)))
                     dsts.append(0)
                 else:
-                    y = torch.empty(shape, dtype=dtype, device=b.device)
+                    y = torch.empty(shape, dtype=dtype, device=b.device) if dest[i] is None else dest[i]
                     dsts.append(y.data_ptr())
                     outs[i] = y
             else:
-                outs[i] = decompress_tensor(b, compute_device=compute_device, readback_to_cpu=readback_to_cpu)
+                outs[i] = decompress_tensor(b, compute_device=compute_device, readback_to_cpu=readback_to_cpu,
+                                            out=dest[i])
         if srcs:
             if tiny:
                 total = sum((nb + 255) & ~255 for _, _, _, nb, _ in tiny)
@@ -843,7 +894,8 @@ def decompress_tensors(
                 x.record_stream(stream)
         ys, meta = [], []
         for i, (dtype, shape, chunk_bytes, n_comp, n) in items:
-            ys.append(torch.empty(shape, dtype=dtype, device=device))
+            y = dest[i] if dest[i] is not None and not readback_to_cpu else None
+            ys.append(torch.empty(shape, dtype=dtype, device=device) if y is None else y)
             meta.append((n, len(shape), chunk_bytes, n_comp))
         nj = len(items)
         n_arr = _ptr_array(ctypes.c_int64, [m[0] for m in meta])
@@ -867,6 +919,10 @@ def decompress_tensors(
 
     for i, blob in enumerate(blobs):
         dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefixes[i][0], prefixes[i][1], plen[i])
+        if dest[i] is not None:
+            _check_out(dest[i], dtype, shape, readback_to_cpu)
+            if dest[i].is_cuda and dest[i].device != _gpu(blob, compute_device):
+                raise ValueError("out is not on the compute device")
         if flags & _FLAG_STORED or n == 0:
             small.append((i, dtype, shape, flags))
             continue
@@ -899,14 +955,15 @@ def decompress_tensors(
         for (k, reorder), (items, _) in cur.items():
             if items:
                 launch(k, reorder, items)
-        _LAST_STATUS[device.index] = status
+        _set_status(device, status)
         decompress_small()
         for ev in uploaded:
             ev.synchronize()
         if readback_to_cpu:
             for i, y in enumerate(outs):
                 if y is not None and y.is_cuda:
-                    host = _populated_empty(y.numel() * y.element_size()).view(y.dtype).view_as(y)
+                    host = dest[i] if dest[i] is not None else (
+                        _populated_empty(y.numel() * y.element_size()).view(y.dtype).view_as(y))
                     host.copy_(y)
                     outs[i] = host
     return outs  # type: ignore[return-value]

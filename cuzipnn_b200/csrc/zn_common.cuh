@@ -3,7 +3,7 @@
 // The codec splits each K-byte element into K byte planes (after the exponent bit reorder that
 // the reference applies to bfloat16 and float32, src/cuzipnn/_kernels.py:17-31) and entropy-codes
 // every (plane, chunk) unit with the ZNR2 interleaved-rANS payload format:
-//   scale 12 bits (M = 4096), u32 states in [2^16, 2^32), 16-bit word I/O, sub-chunks of
+//   scale 12 bits (M = 4096), u32 states in [2^15, 2^31), 16-bit word I/O, sub-chunks of
 //   roundup(ceil(m / n_sub), 128) symbols, each coded by 8 interleaved states with one word
 //   stream each; round r / step i / lane l covers symbol r*128 + l*16 + i of the sub-chunk.
 // The normative CPU statement of the format is oracle/zn_oracle.c; these kernels must produce

@@ -263,9 +263,12 @@ int zn_crc32(const void* data, int64_t nbytes, int64_t segment_bytes, uint32_t* 
     return set_error(ZN_ERR_SPACE, "zn_crc32: temp buffer too small");
   if (nseg * bps > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_crc32: too many blocks");
   uint32_t* partial = static_cast<uint32_t*>(temp);
-  crc_level1<<<unsigned(nseg * bps), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, kThreads, bps, false, out,
-                                                        partial);
-  crc_level2<<<unsigned(nseg), kThreads, 0, st>>>(nbytes, segment_bytes, nseg, bps, partial, out);
+  {
+    TimedLaunch tl("crc", st);  // both levels
+    crc_level1<<<unsigned(nseg * bps), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, kThreads, bps, false, out,
+                                                          partial);
+    crc_level2<<<unsigned(nseg), kThreads, 0, st>>>(nbytes, segment_bytes, nseg, bps, partial, out);
+  }
   count_launch(2);
   return check_launch("zn_crc32");
 }
@@ -283,12 +286,9 @@ int zn_crc32(const void* data, int64_t nbytes, int64_t segment_bytes, uint32_t* 
 // stream order), so nothing needs clearing.  Two calls whose kernels overlap on the GPU (different
 // streams, or host threads with no ordering between them) race on the array.
 
-#include <mutex>
-
 namespace {
 
 constexpr int64_t kNoAllocSlots = int64_t(1) << 19;  // 2 MiB of u32
-constexpr int kNoAllocMaxDevices = 64;
 
 }  // namespace
 
@@ -296,28 +296,17 @@ static __device__ __align__(256) uint32_t g_crc_noalloc_scratch[kNoAllocSlots];
 
 namespace {
 
-std::mutex g_noalloc_mu;
-uint32_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
-
-// Device address of the scratch array on the current device, resolved on the first call per
-// device (this loads the module on that device if it is not loaded yet).
+// Device address of the scratch array in the current device's context.  Looked up on every call
+// (a cheap query once the module is loaded): a cached address would go stale after a
+// cudaDeviceReset, which gives the device a new context.  The first lookup on a device loads the
+// library's device code there.
 int noalloc_scratch(uint32_t** ptr) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(ZN_ERR_CUDA, "zn_crc32_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kNoAllocMaxDevices)
-    return set_error(ZN_ERR_INVALID, "zn_crc32_noalloc: device %d is beyond the %d this entry point supports", dev,
-                     kNoAllocMaxDevices);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_crc_noalloc_scratch);
-    if (e != cudaSuccess || !p)
-      return set_error(ZN_ERR_CUDA, "zn_crc32_noalloc: cudaGetSymbolAddress of the scratch array on device %d: %s",
-                       dev, cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = static_cast<uint32_t*>(p);
-  }
-  *ptr = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_crc_noalloc_scratch);
+  if (e != cudaSuccess || !p)
+    return set_error(ZN_ERR_CUDA, "zn_crc32_noalloc: cudaGetSymbolAddress of the scratch array: %s",
+                     cudaGetErrorString(e));
+  *ptr = static_cast<uint32_t*>(p);
   return ZN_OK;
 }
 
@@ -335,22 +324,26 @@ extern "C" int zn_crc32_noalloc(const void* data, int64_t nbytes, int64_t segmen
                      "zn_crc32_noalloc: %lld bytes in segments of %lld need %lld scratch slots (one per 32 KiB block "
                      "of each segment); the static scratch holds %lld (2 MiB). Use zn_crc32 with a temp buffer",
                      (long long)nbytes, (long long)segment_bytes, (long long)(nseg * bps), (long long)kNoAllocSlots);
-  uint32_t* partial = nullptr;
-  if (int rc = noalloc_scratch(&partial)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint8_t* d = static_cast<const uint8_t*>(data);
-  if (bps == 0) {  // every segment fits one CTA: the scratch is not touched
+  if (bps == 0) {  // every segment fits one CTA: the scratch is neither touched nor looked up
     int G = 1;
     while (int64_t(G) * kPiece < seg) G <<= 1;
     const int64_t grid = cdiv(nseg, int64_t(kThreads / G));
     if (grid > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_crc32_noalloc: too many segments");
+    TimedLaunch tl("crc", st);
     crc_level1<<<unsigned(grid), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, G, 1, true, out, nullptr);
     count_launch();
     return check_launch("zn_crc32_noalloc");
   }
-  crc_level1<<<unsigned(nseg * bps), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, kThreads, bps, false, out,
-                                                        partial);
-  crc_level2<<<unsigned(nseg), kThreads, 0, st>>>(nbytes, segment_bytes, nseg, bps, partial, out);
+  uint32_t* partial = nullptr;
+  if (int rc = noalloc_scratch(&partial)) return rc;
+  {
+    TimedLaunch tl("crc", st);
+    crc_level1<<<unsigned(nseg * bps), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, kThreads, bps, false, out,
+                                                          partial);
+    crc_level2<<<unsigned(nseg), kThreads, 0, st>>>(nbytes, segment_bytes, nseg, bps, partial, out);
+  }
   count_launch(2);
   return check_launch("zn_crc32_noalloc");
 }

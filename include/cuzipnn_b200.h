@@ -4,8 +4,10 @@
  * Every entry point takes plain pointers and sizes, works on caller-owned device memory, allocates
  * nothing, enqueues its work on the given CUDA stream (a cudaStream_t passed as void*; NULL is the
  * legacy default stream) on the current device, and returns ZN_OK or a negative status.
- * zn_last_error() describes the last failure of the calling thread.  Calls are reentrant: all
- * state lives in the caller's buffers.
+ * zn_last_error() describes the last failure of the calling thread.  Calls are reentrant: their
+ * state lives in the caller's buffers, with two exceptions: zn_crc32_noalloc's scratch is one
+ * static device array that every call on a device shares (see its declaration), and the opt-in
+ * kernel timing (zn_timing_*) keeps one process-wide list of events.
  *
  * The reference (ruihe774/cuZipNN) is a Python package whose GPU work goes through two internal
  * seams: Triton kernels (src/cuzipnn/_kernels.py) and ctypes bindings of NVIDIA nvCOMP
@@ -103,9 +105,10 @@ int zn_crc32(const void *data, int64_t nbytes, int64_t segment_bytes, uint32_t *
  * nothing: its scratch is one fixed 2 MiB array of device memory (524,288 slots, one per 32 KiB
  * block of each segment longer than 32 KiB, e.g. up to 16 GiB of data in segments that are a
  * multiple of 32 KiB), which every GPU that runs it holds until the process exits.  A call that
- * needs more slots returns ZN_ERR_INVALID and launches nothing.  The first call on each device
- * looks up the array's address there (loading the library's device code if needed), so make that
- * first call before any stream capture.  All calls on a device share the array: calls whose
+ * needs more slots returns ZN_ERR_INVALID and launches nothing.  Every call that uses the array
+ * looks up its address in the current device's context (so the address stays right after a
+ * cudaDeviceReset); the first such call on a device loads the library's device code there, so
+ * make it before any stream capture.  All calls on a device share the array: calls whose
  * kernels overlap on the GPU (other streams, or host threads with no ordering between them) race
  * and return wrong CRCs.  Segments of at most 32 KiB do not touch the array. */
 int zn_crc32_noalloc(const void *data, int64_t nbytes, int64_t segment_bytes, uint32_t *out, void *stream);

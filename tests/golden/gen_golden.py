@@ -2,7 +2,7 @@
 
 Run (in a container that has the reference checkout; nothing else reads it):
 
-    python tests/golden/gen_golden.py [/path/to/cuZipNN]
+    python tests/golden/gen_golden.py /path/to/cuZipNN
 
 It imports, from the reference checkout (ruihe774/cuZipNN):
   - src/cuzipnn/_kernels.py, run by Triton's CPU interpreter (TRITON_INTERPRET=1), for the
@@ -295,4 +295,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: gen_golden.py /path/to/cuZipNN (the reference checkout)")
+    main(sys.argv[1])

@@ -3,7 +3,9 @@ tensor round-trips bit for bit, the compression ratio sits just above the order-
 the synthetic weights (the same bound the reference's nvCOMP coder is held to), CRCs of the blobs
 verify, and sampled tensors equal the oracle's blobs byte for byte.
 
-The 7B bf16 decoder is the benchmark workload itself (bench.py checks it every run)."""
+The 7B bf16 decoder (the benchmark workload) is checked the same way: every tensor through the
+batched calls and through compress_tensor one at a time, and the oracle's blobs for a q_proj, a
+down_proj, a stored norm and a 16-chunk range of the embedding."""
 
 import math
 import os
@@ -126,3 +128,31 @@ def test_dtype_sweep_64mib_uniform(dtype):
         assert 0.12 < ratio < 0.135, ratio
     else:
         assert 0.99 < ratio < 1.001, ratio
+
+
+def test_config2_7b_bf16_headline():
+    """The 7B GQA decoder in bf16 (339 tensors, 15.23 GB), the workload bench.py measures."""
+    import bench
+
+    shapes = bench.model_shapes()
+    model = bench.build_model("cuda")
+    assert len(model) == 339 and abs(_nbytes(model) - 15.23e9) < 0.01e9
+    blobs = _round_trip(model)
+    ratio = sum(b.numel() for b in blobs) / _nbytes(model)
+    assert 0.661 < ratio < 0.663, ratio  # order-0 bound of N(0, 0.02) bf16: 65.91 %
+    # compress_tensor one tensor at a time gives the same blobs as the batched call.
+    for i, x in enumerate(model):
+        assert torch.equal(z.compress_tensor(x, readback_to_cpu=False), blobs[i]), i
+    names = [n for n, _, _ in shapes]
+    q = names.index("model.layers.3.self_attn.q_proj.weight")
+    down = names.index("model.layers.27.mlp.down_proj.weight")
+    norm = names.index("model.layers.5.input_layernorm.weight")
+    assert blobs[norm].numel() == 24 + 8 + 3584 * 2  # the stored path
+    _oracle_check(model, blobs, [q, down, norm])
+    # Chunks 2000 .. 2015 of the embedding (152064 x 3584): the oracle's blob of those elements.
+    emb = names.index("model.embed_tokens.weight")
+    j0, j1, C = 2000, 2016, 131072
+    part = z.split_chunk_range(blobs[emb], j0, j1)
+    raw = model[emb].view(-1)[j0 * C : j1 * C].cpu().view(torch.uint8).numpy()
+    ref = O.compress(raw, (raw.size // 2,), "bfloat16", min_compress_bytes=0, threads=os.cpu_count() or 1)
+    assert np.array_equal(part.cpu().numpy(), np.frombuffer(ref, dtype=np.uint8))

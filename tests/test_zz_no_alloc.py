@@ -7,10 +7,14 @@ array in device memory that all calls share and that keeps the previous call's c
 
 The GPU test calls it through the C ABI twice in a row, on different sizes and segment lengths,
 and requires the same CRCs (bit for bit) as zn_crc32 with a caller-allocated temp buffer, and as
-zlib.  It must pass alone in a fresh process (the first call then also does the per-device set-up)
-and after the other tests; the file name makes pytest collect it last.
+zlib.  It must pass alone in a fresh process (the first call then also loads the device code) and
+after the other tests: the file name makes pytest collect it last, and one test re-runs it in a
+fresh Python process.
 """
 
+import os
+import subprocess
+import sys
 import zlib
 
 import numpy as np
@@ -71,3 +75,55 @@ def test_noalloc_crc_rejects_sizes_beyond_its_scratch():
     assert _lib.lib.zn_crc32_noalloc(None, -1, 4096, None, None) == _lib.ZN_ERR_INVALID
     assert _lib.lib.zn_crc32_noalloc(None, 10, 0, None, None) == _lib.ZN_ERR_INVALID
     assert _lib.lib.zn_crc32_noalloc(None, 0, 4096, None, None) == _lib.ZN_OK
+
+
+@pytest.mark.gpu
+def test_noalloc_crc_in_a_fresh_process():
+    """The consecutive-calls test again, alone in a new Python process."""
+    node = os.path.abspath(__file__) + "::test_noalloc_crc_equals_zn_crc32_on_consecutive_calls"
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider", node],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "1 passed" in r.stdout
+
+
+@pytest.mark.gpu
+def test_noalloc_crc_at_exactly_the_scratch_size():
+    """2^18 segments of 32 KiB + 1 bytes need exactly 2^19 scratch slots (two blocks each): accepted,
+    and equal to zn_crc32."""
+    seg = 32768 + 1
+    nseg = SCRATCH_SLOTS // 2
+    nbytes = seg * nseg
+    stream = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device="cuda").manual_seed(9)
+    buf = torch.randint(0, 256, (nbytes,), generator=g, device="cuda", dtype=torch.uint8)
+    ref = _crc_with_temp(buf, seg, stream)
+    out = torch.zeros_like(ref)
+    _lib.check(_lib.lib.zn_crc32_noalloc(buf.data_ptr(), nbytes, seg, out.data_ptr(), stream), "zn_crc32_noalloc")
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    host = buf[-2 * seg:].cpu().numpy()
+    assert out[-2:].cpu().numpy().view(np.uint32).tolist() == [zlib.crc32(host[:seg].tobytes()),
+                                                              zlib.crc32(host[seg:].tobytes())]
+    del buf
+    # One byte more adds a segment of one byte, which needs two more slots: refused.
+    assert _lib.lib.zn_crc32_noalloc(None, nbytes + 1, seg, None, None) == _lib.ZN_ERR_INVALID
+
+
+def test_noalloc_crc_boundary_on_the_host():
+    """The size check at the limit, with null pointers (nothing may be launched): one slot over the
+    limit is refused with the scratch message, and a call at exactly the limit passes that check."""
+    before = _lib.launch_count()
+    # 2^19 + 1 slots: 2^19 + 1 segments of 32 KiB + 1 bytes would be 2 slots each, so use one
+    # segment of (2^19 + 1) * 32 KiB bytes: one slot per 32 KiB block.
+    over = (SCRATCH_SLOTS + 1) * 32768
+    assert _lib.lib.zn_crc32_noalloc(None, over, over, None, None) == _lib.ZN_ERR_INVALID
+    assert "scratch" in _lib.lib.zn_last_error().decode()
+    assert _lib.launch_count() == before
+    if torch.cuda.is_available():
+        return  # at the limit the call would go on to launch on the null pointers
+    at = SCRATCH_SLOTS * 32768
+    rc = _lib.lib.zn_crc32_noalloc(None, at, at, None, None)
+    assert rc != _lib.ZN_OK  # no GPU here: the symbol lookup fails, after the size check
+    assert "need" not in _lib.lib.zn_last_error().decode()
+    assert _lib.launch_count() == before
