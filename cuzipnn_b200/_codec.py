@@ -121,7 +121,34 @@ def _gpu(x: torch.Tensor, compute_device: torch.device | None) -> torch.device:
 
 
 def _stream(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """Raw handle of the device's current stream (as torch.cuda.current_stream(device).cuda_stream,
+    without building a Stream object on every call)."""
+    return torch._C._cuda_getCurrentRawStream(device.index)
+
+
+def _on(device: torch.device):
+    """torch.cuda.device(device), or nothing when it is the current device already."""
+    if torch.cuda.current_device() == device.index:
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
+
+
+def _remember(blob: torch.Tensor, dtype: torch.dtype, shape: tuple[int, ...], flags: int, chunk_bytes: int,
+              n: int) -> torch.Tensor:
+    """Keep the header fields of a GPU blob made here on the returned tensor object, with the
+    blob's version counter, address and size: decompressing the unchanged blob then needs no host
+    read of its header (a synchronization that would drain the stream).  Any in-place write to
+    the blob or to a view of its storage bumps the shared version counter and voids the record."""
+    blob._zn_header = (blob._version, blob.data_ptr(), blob.numel(), dtype, shape, flags, chunk_bytes, n)
+    return blob
+
+
+def _known_header(blob: torch.Tensor):
+    """(dtype, shape, flags, chunk_bytes, n) of a GPU blob from _remember, if it still applies."""
+    h = getattr(blob, "_zn_header", None)
+    if h is None or not blob.is_cuda or h[0] != blob._version or h[1] != blob.data_ptr() or h[2] != blob.numel():
+        return None
+    return h[3:]
 
 
 def _crc32(data: torch.Tensor, checksum_chunk_bytes: int) -> torch.Tensor:
@@ -312,16 +339,19 @@ def _compress(
             blob[:header_size].copy_(torch.frombuffer(bytearray(head), dtype=torch.uint8))
             return _fill_stored(blob, header_size, x, checksum_chunk_bytes)
         device = _gpu(x, compute_device)
-        with torch.cuda.device(device):
+        with _on(device):
             blob = torch.empty(header_size + n * k, dtype=torch.uint8, device=device)
             blob[:header_size].copy_(torch.frombuffer(bytearray(head), dtype=torch.uint8))
             blob[header_size:].view(x.dtype).view(x.shape).copy_(x)
             crc = None if checksum_chunk_bytes is None else _crc32(blob, checksum_chunk_bytes)
-            return blob, crc
+            flags = _FLAG_STORED if stored else _FLAG_REORDER if reorder else 0
+            return _remember(blob, x.dtype, tuple(x.shape), flags, 0 if stored else chunk_bytes, n), crc
 
     device = _gpu(x, compute_device)
-    with torch.cuda.device(device):
-        x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous().view(-1)
+    with _on(device):
+        if not (x.device == device and x.is_contiguous()):
+            x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+        x = x.view(-1)
         if x.data_ptr() % 16:
             x = x.clone()
         head = _header(tensor, _FLAG_REORDER if reorder else 0, chunk_bytes, 0)
@@ -345,7 +375,8 @@ def _compress(
         if checksum_chunk_bytes is not None:
             crc = _crc32(comp, checksum_chunk_bytes)
         if not readback_to_cpu:
-            return comp, crc
+            return _remember(comp, tensor.dtype, tuple(tensor.shape), _FLAG_REORDER if reorder else 0, chunk_bytes,
+                             n), crc
         blob = _populated_empty(size, pin_memory=pin_memory)
         # With a crc, crc.cpu() below syncs the stream, so blob is complete on return.
         blob.copy_(comp, non_blocking=crc is not None)
@@ -434,11 +465,16 @@ def decompress_tensor(
     if blob.dtype != torch.uint8 or blob.dim() != 1:
         raise ValueError("blob must be a 1-D uint8 tensor")
 
+    known = _known_header(blob)
     blob = blob.detach()
-    prefix_len = min(blob.numel(), _FIXED.size + 8 * _MAX_NDIM)
-    prefix_tensor = blob[:prefix_len].to("cpu", memory_format=torch.contiguous_format).contiguous()
-    prefix = (ctypes.c_byte * prefix_len).from_address(prefix_tensor.data_ptr())
-    dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefix)
+    if known is not None:  # an unchanged GPU blob made here: its header is on the host already
+        dtype, shape, flags, chunk_bytes, n = known
+        n_comp = -1  # read from the blob by the device
+    else:
+        prefix_len = min(blob.numel(), _FIXED.size + 8 * _MAX_NDIM)
+        prefix_tensor = blob[:prefix_len].to("cpu", memory_format=torch.contiguous_format).contiguous()
+        prefix = (ctypes.c_byte * prefix_len).from_address(prefix_tensor.data_ptr())
+        dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefix)
     reorder = bool(flags & _FLAG_REORDER)
     if out is not None:
         _check_out(out, dtype, shape, readback_to_cpu)
@@ -474,14 +510,16 @@ def decompress_tensor(
     y = out if (out is not None and not readback_to_cpu) else torch.empty(shape, dtype=dtype, device=device)
 
     k = y.element_size()
-    nch = -(-n // chunk_bytes)
-    total = k * nch
-    _, _, data_off = _layout(len(shape), total, n_comp)
-    if blob.numel() < data_off:
-        raise ValueError("blob is truncated")
+    if n_comp >= 0:
+        nch = -(-n // chunk_bytes)
+        _, _, data_off = _layout(len(shape), k * nch, n_comp)
+        if blob.numel() < data_off:
+            raise ValueError("blob is truncated")
 
-    with torch.cuda.device(device):
-        x = blob.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+    with _on(device):
+        x = blob
+        if not (x.device == device and x.is_contiguous()):
+            x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
         if x.data_ptr() % 8:
             x = x.clone()
         # A pinned blob is uploaded asynchronously, but the caller may reuse it once we return.
@@ -490,7 +528,7 @@ def decompress_tensor(
             uploaded.record()
         temp_bytes = int(_lib.lib.zn_decompress_temp_bytes(n, k, chunk_bytes))
         temp = torch.empty(max(temp_bytes, 1), dtype=torch.uint8, device=device)
-        status = torch.zeros(1, dtype=torch.int32, device=device)
+        status = torch.empty(1, dtype=torch.int32, device=device)  # set by the call
         _lib.check(
             _lib.lib.zn_decompress(
                 x.data_ptr(), x.numel(), n, k, int(reorder), len(shape), chunk_bytes, n_comp,
@@ -628,7 +666,10 @@ def compress_tensors(
                                            compute_device=compute_device, readback_to_cpu=readback_to_cpu)
         if batch:
             for i, b in _stored_blobs_gpu(batch, device).items():
-                blobs[i] = b
+                t = tensors[i]
+                stored = t.numel() * t.element_size() < min_compress_bytes
+                flags = _FLAG_STORED if stored else _FLAG_REORDER if t.dtype in _REORDER else 0
+                blobs[i] = _remember(b, t.dtype, tuple(t.shape), flags, 0 if stored else chunk_bytes, t.numel())
 
     device: torch.device | None = None
     stream = copy_in = None
@@ -721,7 +762,9 @@ def compress_tensors(
                     pieces += (size, nxt - o - size)
                 views = out.split(pieces)
                 for j, i in enumerate(idx):
-                    blobs[i] = views[2 * j]
+                    t = tensors[i]
+                    blobs[i] = _remember(views[2 * j], t.dtype, tuple(t.shape),
+                                         _FLAG_REORDER if t.dtype in _REORDER else 0, chunk_bytes, t.numel())
                 pos += len(idx)
             return blobs  # type: ignore[return-value]
         copy_out = _side_stream(device, 1)
@@ -802,13 +845,19 @@ def decompress_tensors(
     dest = list(out) if out is not None else [None] * len(blobs)
     outs: list[torch.Tensor | None] = [None] * len(blobs)
     # Headers of GPU blobs come to the host in one copy per device; prefixes[i] = (buffer, offset).
+    # Unchanged GPU blobs made by this module carry their header fields (_remember); only the others
+    # are read back.
     plen = [0] * len(blobs)
     prefixes: list[tuple[memoryview, int] | None] = [None] * len(blobs)
+    known = [None] * len(blobs)
     by_dev: dict[torch.device, list[int]] = {}
     for i, blob in enumerate(blobs):
         if blob.dtype != torch.uint8 or blob.dim() != 1:
             raise ValueError("blob must be a 1-D uint8 tensor")
         plen[i] = p = min(blob.numel(), _FIXED.size + 8 * _MAX_NDIM)
+        known[i] = _known_header(blob)
+        if known[i] is not None:
+            continue
         if blob.is_cuda:
             by_dev.setdefault(blob.device, []).append(i)
         else:
@@ -918,7 +967,11 @@ def decompress_tensors(
             outs[i] = y
 
     for i, blob in enumerate(blobs):
-        dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefixes[i][0], prefixes[i][1], plen[i])
+        if known[i] is not None:
+            dtype, shape, flags, chunk_bytes, n = known[i]
+            n_comp = -1  # read from the blob by the device
+        else:
+            dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefixes[i][0], prefixes[i][1], plen[i])
         if dest[i] is not None:
             _check_out(dest[i], dtype, shape, readback_to_cpu)
             if dest[i].is_cuda and dest[i].device != _gpu(blob, compute_device):
@@ -929,10 +982,11 @@ def decompress_tensors(
         if math.prod(shape) != n or chunk_bytes <= 0:
             raise ValueError("not a cuzipnn blob")
         k = dtype.itemsize
-        nch = -(-n // chunk_bytes)
-        _, _, data_off = _layout(len(shape), k * nch, n_comp)
-        if blob.numel() < data_off:
-            raise ValueError("blob is truncated")
+        if n_comp >= 0:
+            nch = -(-n // chunk_bytes)
+            _, _, data_off = _layout(len(shape), k * nch, n_comp)
+            if blob.numel() < data_off:
+                raise ValueError("blob is truncated")
         if device is None:
             device = _gpu(blob, compute_device)
             stream = torch.cuda.current_stream(device)

@@ -1,5 +1,7 @@
-// Host-side plumbing of the C ABI: version, per-thread error messages, launch counter and the
-// opt-in for large dynamic shared memory.
+// Host-side plumbing of the C ABI: version, per-thread error messages, launch counter, the opt-in
+// for large dynamic shared memory, NVTX ranges and the opt-in kernel timing.
+#include <nvtx3/nvToolsExt.h>
+
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -71,7 +73,11 @@ struct Timing {
 };
 static Timing g_timing;
 
+NvtxScope::NvtxScope(const char* name) { nvtxRangePushA(name); }
+NvtxScope::~NvtxScope() { nvtxRangePop(); }
+
 TimedLaunch::TimedLaunch(const char* kernel, cudaStream_t s) : slot(-1), stream(s) {
+  nvtxRangePushA(kernel);  // a host range around each kernel stage's launch (no-op without a tool)
   std::lock_guard<std::mutex> lock(g_timing.mu);
   if (g_timing.kernel.empty() || (g_timing.kernel != "*" && g_timing.kernel != kernel)) return;
   std::pair<cudaEvent_t, cudaEvent_t> ev;
@@ -87,6 +93,7 @@ TimedLaunch::TimedLaunch(const char* kernel, cudaStream_t s) : slot(-1), stream(
 }
 
 TimedLaunch::~TimedLaunch() {
+  nvtxRangePop();
   if (slot < 0) return;
   std::lock_guard<std::mutex> lock(g_timing.mu);
   if (slot < int(g_timing.pending.size())) cudaEventRecord(g_timing.pending[slot].stop, stream);

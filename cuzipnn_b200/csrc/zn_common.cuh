@@ -284,8 +284,15 @@ int upload_jobs(const T* host, int count, T* dev, int64_t total_chunks, cudaStre
   return ZN_OK;
 }
 
+// An NVTX range over a scope of host code (entry points), visible to Nsight tools.
+struct NvtxScope {
+  explicit NvtxScope(const char* name);
+  ~NvtxScope();
+};
+
 // Opt-in event timing of one kernel kind (zn_timing_enable): bracket a launch with
-// TimedLaunch t("decode", stream); ... launch ...; (the destructor records the end event).
+// TimedLaunch t("decode", stream); ... launch ...; (the destructor records the end event).  It
+// also opens an NVTX range named after the kernel kind for the launch.
 struct TimedLaunch {
   TimedLaunch(const char* kernel, cudaStream_t stream);
   ~TimedLaunch();

@@ -414,7 +414,8 @@ __device__ __forceinline__ void decode_chunk(const DecArgs* __restrict__ jobs, i
     } else {
       const int64_t u = int64_t(tid) * a.nch + j;
       const int64_t s = a.src[u];
-      const int64_t stored = *reinterpret_cast<const int32_t*>(a.blob + a.sizes_off + 4 * u);
+      // dscan_kernel has checked that the tables lie inside the blob for every unit with s >= 0.
+      const int64_t stored = s >= 0 ? *reinterpret_cast<const int32_t*>(a.blob + a.sizes_off + 4 * u) : 0;
       P.coded = s >= 0 && (s & kCodedBit);
       P.pl = a.blob + (s & kOffMask);
       P.size = stored;
@@ -755,14 +756,31 @@ __global__ void __launch_bounds__(kDecThreads) decode_overflow_kernel(const DecA
 
 constexpr int kScanThreads = 1024;
 
-// One CTA per job.
+// One CTA per job.  It first zeroes the job's status word.  A job whose n_comp is negative reads
+// it from the blob's header (u32 at byte 12) here; tables that do not fit the blob then mark every
+// unit invalid (the decoder zero-fills them) and set kErrTable.
 __global__ void __launch_bounds__(kScanThreads) dscan_kernel(const DecArgs* __restrict__ jobs) {
   __shared__ int64_t sm[64];
+  __shared__ int64_t s_ncomp;
   const DecArgs& a = jobs[blockIdx.x];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (tid == 0) {
+    *a.status = 0;
+    int64_t nc = a.n_comp;
+    if (nc < 0) nc = a.blob_bytes >= 16 ? int64_t(*reinterpret_cast<const uint32_t*>(a.blob + 12)) : -1;
+    s_ncomp = nc;
+  }
+  __syncthreads();
+  const int64_t n_comp = s_ncomp;
+  const int64_t data_off = align8(a.idx_off + 4 * n_comp);
+  if (n_comp < 0 || n_comp > a.units || data_off > a.blob_bytes) {
+    for (int64_t i = tid; i < a.units; i += kScanThreads) a.src[i] = -1;
+    if (tid == 0) atomicOr(a.status, kErrTable);
+    return;
+  }
   const int64_t last = a.n - (a.nch - 1) * a.C;
   const int32_t* stored = reinterpret_cast<const int32_t*>(a.blob + a.sizes_off);
-  int64_t carry = a.data_off;
+  int64_t carry = data_off;
   bool bad = false;
   for (int64_t start = 0; start < a.units; start += kScanThreads) {
     const int64_t i = start + tid;
@@ -795,7 +813,7 @@ __global__ void __launch_bounds__(kScanThreads) dscan_kernel(const DecArgs* __re
   }
   __syncthreads();
   const int32_t* idx = reinterpret_cast<const int32_t*>(a.blob + a.idx_off);
-  for (int64_t q = tid; q < a.n_comp; q += kScanThreads) {
+  for (int64_t q = tid; q < n_comp; q += kScanThreads) {
     const int64_t i = idx[q];
     if (i < 0 || i >= a.units) { bad = true; continue; }
     a.src[i] |= kCodedBit;
@@ -906,6 +924,7 @@ int zn_decompress_batch(int njobs, const void* const* blobs, const int64_t* blob
   if (njobs < 0 || (k != 1 && k != 2 && k != 4 && k != 8) || (reorder && k != 2 && k != 4))
     return set_error(ZN_ERR_INVALID, "zn_decompress: bad arguments");
   if (njobs == 0) return ZN_OK;
+  NvtxScope range("zn_decompress_batch");
   if (!temp || temp_bytes < zn_decompress_batch_temp_bytes(njobs, n, k, chunk_bytes))
     return set_error(ZN_ERR_SPACE, "zn_decompress: temp buffer too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -917,7 +936,7 @@ int zn_decompress_batch(int njobs, const void* const* blobs, const int64_t* blob
   jobs.reserve(static_cast<size_t>(njobs));
   int64_t chunk0 = 0;
   for (int i = 0; i < njobs; ++i) {
-    if (n[i] < 0 || chunk_bytes[i] <= 0 || ndim[i] < 0 || ndim[i] > 64 || n_comp[i] < 0 ||
+    if (n[i] < 0 || chunk_bytes[i] <= 0 || ndim[i] < 0 || ndim[i] > 64 || n_comp[i] < -1 ||
         (reinterpret_cast<uintptr_t>(blobs[i]) & 7))
       return set_error(ZN_ERR_INVALID, "zn_decompress: bad arguments (job %d)", i);
     if (n[i] == 0) continue;
@@ -931,9 +950,10 @@ int zn_decompress_batch(int njobs, const void* const* blobs, const int64_t* blob
     if (a.nch > 0x7FFFFFFF || n_comp[i] > a.units) return set_error(ZN_ERR_INVALID, "zn_decompress: bad tables (job %d)", i);
     a.sizes_off = 24 + 8 * int64_t(ndim[i]);
     a.idx_off = a.sizes_off + 4 * a.units;
-    a.n_comp = n_comp[i];
-    a.data_off = align8(a.idx_off + 4 * a.n_comp);
-    if (a.blob_bytes < a.data_off) return set_error(ZN_ERR_INVALID, "zn_decompress: blob is truncated (job %d)", i);
+    a.n_comp = n_comp[i];  // -1: dscan_kernel reads it from the blob
+    a.data_off = n_comp[i] < 0 ? -1 : align8(a.idx_off + 4 * a.n_comp);
+    if (n_comp[i] >= 0 && a.blob_bytes < a.data_off)
+      return set_error(ZN_ERR_INVALID, "zn_decompress: blob is truncated (job %d)", i);
     a.chunk0 = chunk0;
     a.out = static_cast<uint8_t*>(out[i]);
     a.status = status + i;

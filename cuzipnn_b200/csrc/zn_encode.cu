@@ -1341,6 +1341,7 @@ int zn_compress_batch(int njobs, const void* const* x, const int64_t* n, int k, 
       chunk_bytes % 8 || !(threshold > 0.0 && threshold <= 1.0))
     return set_error(ZN_ERR_INVALID, "zn_compress: bad arguments");
   if (njobs == 0) return ZN_OK;
+  NvtxScope range("zn_compress_batch");
   if (!temp || temp_bytes < zn_compress_batch_temp_bytes(njobs, n, k, chunk_bytes, sub_chunks))
     return set_error(ZN_ERR_SPACE, "zn_compress: temp buffer too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -138,14 +138,17 @@ int zn_compress_batch(int njobs, const void *const *x, const int64_t *n, int k, 
 
 size_t zn_decompress_temp_bytes(int64_t n, int k, int64_t chunk_bytes);
 /* Decompress the non-stored blob at blob (device, 8-byte aligned, blob_bytes long) whose header
- * fields are given, into out (n * k bytes, device).  Decoding errors are OR-ed into the device
- * int32 at status (which the caller zeroes); the kernels never read or write out of bounds. */
+ * fields are given, into out (n * k bytes, device).  n_comp may be -1: the device then reads it
+ * from the blob's header, so a caller that knows the other fields needs no host read of the blob.
+ * The call sets the device int32 at status: 0, then the OR of the decoding errors; the kernels
+ * never read or write out of bounds. */
 int zn_decompress(const void *blob, int64_t blob_bytes, int64_t n, int k, int reorder, int ndim,
                   int64_t chunk_bytes, int64_t n_comp, void *out, int32_t *status, void *temp,
                   size_t temp_bytes, void *stream);
 
 /* Batched form of zn_decompress: njobs non-stored blobs of one element size (host arrays, one
- * entry per blob; status is a device array of njobs int32 that the caller zeroes). */
+ * entry per blob; status is a device array of njobs int32, set as in zn_decompress for every job
+ * with n > 0 and left as it is for jobs with n = 0). */
 size_t zn_decompress_batch_temp_bytes(int njobs, const int64_t *n, int k, const int64_t *chunk_bytes);
 int zn_decompress_batch(int njobs, const void *const *blobs, const int64_t *blob_bytes, const int64_t *n, int k,
                         int reorder, const int *ndim, const int64_t *chunk_bytes, const int64_t *n_comp,

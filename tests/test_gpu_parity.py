@@ -263,3 +263,50 @@ def test_raw_planes_in_place_guess_right_and_wrong(z, dtype):
         blob = z.compress_tensor(x.cuda(), chunk_bytes=C, min_compress_bytes=0)
         assert np.array_equal(_u8(blob), np.frombuffer(ref, dtype=np.uint8)), name
         assert np.array_equal(_u8(z.decompress_tensor(blob)), _u8(x)), name
+
+
+def test_remembered_header_voided_by_in_place_writes(z):
+    """GPU blobs made here carry their header fields, so decompressing them reads nothing back to
+    the host; an in-place write to the blob (or a view of it) voids that record, so a damaged
+    header is still caught, and damaged tables are reported through the status word."""
+    x = (torch.randn(300_000, device="cuda") * 0.02).to(torch.bfloat16)
+    for make in (lambda: z.compress_tensor(x, readback_to_cpu=False, chunk_bytes=65536),
+                 lambda: z.compress_tensors([x, x[:1000]], readback_to_cpu=False, chunk_bytes=65536)[0]):
+        blob = make()
+        assert torch.equal(z.decompress_tensor(blob).view(torch.int16), x.view(torch.int16))
+        assert torch.equal(z.decompress_tensors([blob])[0].view(torch.int16), x.view(torch.int16))
+        blob[0] = 0  # the magic, through the tensor: the record no longer applies
+        with pytest.raises(ValueError, match="not a cuzipnn blob"):
+            z.decompress_tensor(blob)
+        with pytest.raises(ValueError, match="not a cuzipnn blob"):
+            z.decompress_tensors([blob])
+        blob2 = make()
+        blob2[12:16].view(torch.int32).fill_(1 << 30)  # n_comp far beyond the blob, via a view
+        with pytest.raises(ValueError, match="truncated"):
+            z.decompress_tensor(blob2)
+
+
+def test_device_read_n_comp_with_truncated_blob(z):
+    """zn_decompress with n_comp = -1 reads it from the blob on the device; tables that do not fit
+    the blob are reported (kErrTable) and the output is zero-filled, with no fault."""
+    from cuzipnn_b200 import _lib
+
+    x = (torch.randn(200_000, device="cuda") * 0.02).to(torch.bfloat16)
+    blob = z.compress_tensor(x, readback_to_cpu=False)
+    n, k = x.numel(), 2
+    s = torch.cuda.current_stream().cuda_stream
+    tb = _lib.lib.zn_decompress_temp_bytes(n, k, 131072)
+    temp = torch.empty(tb, dtype=torch.uint8, device="cuda")
+    status = torch.full((1,), 123, dtype=torch.int32, device="cuda")
+    for nbytes, want in ((blob.numel(), 0), (40, 4), (8, 4)):  # 4: the table error bit
+        out = torch.full_like(x, 1.0)
+        rc = _lib.lib.zn_decompress(blob.data_ptr(), nbytes, n, k, 1, 1, 131072, -1, out.data_ptr(),
+                                    status.data_ptr(), temp.data_ptr(), tb, s)
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert int(status.item()) & 4 == want, nbytes
+        if want == 0:
+            assert int(status.item()) == 0
+            assert torch.equal(out.view(torch.int16), x.view(torch.int16))
+        else:
+            assert int((out.view(torch.int16) != 0).sum()) == 0
