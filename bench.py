@@ -186,6 +186,56 @@ def cpu_sample(device="cpu") -> list[torch.Tensor]:
     return [make_tensor(i, s, init, device) for i, (n, s, init) in enumerate(shapes) if ".layers.0." in n]
 
 
+# ---- micro-benchmarks of the seam and CRC kernels ----------------------------------------------
+
+
+def micro_benchmarks(device, reps: int = 10) -> dict:
+    """Device time (CUDA events, mean of `reps` after 3 warm-up calls) of the byte-plane seam
+    kernels on 1 GiB of bf16 N(0, 0.02) (zn_split with the exponent reorder into planes of stride
+    nch * 131072, zn_merge back, checked bit for bit) and of zn_crc32 on 1 GiB of random bytes in
+    16 KiB segments.  Rates are algorithmic bytes (split / merge: read + write; CRC: read) per
+    second, inputs larger than L2."""
+    from cuzipnn_b200 import _codec as C
+    from cuzipnn_b200 import _kernels as K
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps / 1e3
+
+    n, chunk = 1 << 29, 131072
+    g = torch.Generator(device=device).manual_seed(11)
+    x = (torch.randn(n, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    nch = -(-n // chunk)
+    stride = nch * chunk
+    planar = torch.empty(2 * stride, dtype=torch.uint8, device=device)
+    tbl = torch.tensor([b * stride + j * chunk for b in range(2) for j in range(nch)], dtype=torch.int64, device=device)
+    y = torch.empty_like(x)
+    t_split = timed(lambda: K.split(x, planar, stride, True))
+    t_merge = timed(lambda: K.merge(tbl, planar, y, chunk, True))
+    assert torch.equal(y.view(torch.int16), x.view(torch.int16))
+    del planar, tbl, y
+    data = torch.randint(0, 256, (1 << 30,), generator=g, device=device, dtype=torch.uint8)
+    t_crc = timed(lambda: C._crc32(data, 16384))
+    del data, x
+    peak, _ = measured_hbm_peak()
+    out = {}
+    for name, nbytes, t in (("split", 4 * n, t_split), ("merge", 4 * n, t_merge), ("crc", 1 << 30, t_crc)):
+        gbs = nbytes / t / GB
+        out[name] = {"gbs": round(gbs, 1), "ms": round(t * 1e3, 4), "frac_of_measured_hbm": round(gbs / peak, 4),
+                     "frac_of_8tbs_nominal": round(gbs / 8000, 4)}
+    out["workload"] = ("split / merge: 2^29 bf16 (1 GiB), reorder, chunk 131072, read + write bytes; "
+                       "crc: 1 GiB random bytes, 16 KiB segments, bytes read")
+    return out
+
+
 # ---- the reference arm --------------------------------------------------------------------------
 
 
@@ -240,6 +290,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-one-at-a-time", action="store_true")
+    ap.add_argument("--micro-only", action="store_true",
+                    help="run only the seam and CRC micro-benchmarks and print their JSON")
+    ap.add_argument("--no-micro", action="store_true")
     ap.add_argument("--layers", type=int, default=None,
                     help="profile a smaller model: this many decoder layers, no embedding / LM head")
     args = ap.parse_args()
@@ -275,6 +328,14 @@ def main() -> None:
         t = torch.tensor([v], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if args.micro_only:
+        m = micro_benchmarks(device)
+        if rank == 0:
+            print(json.dumps({"micro": m}), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     model = build_model(device, args.layers)
     model_bytes = nbytes(model)
@@ -431,6 +492,8 @@ def main() -> None:
                "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e * 1e3, 1),
                "path": "pinned host tensors -> compress_tensors(readback_to_cpu, pin_memory) -> decompress_tensors"}
 
+    micro = None if args.no_micro else micro_benchmarks(device)
+
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -472,6 +535,7 @@ def main() -> None:
             "clocks": clocks.summary(),
             "e2e": e2e,
             "sharded": sharded,
+            "micro": micro,
             "gpu_launches": gpu_launches,
         }
         print(json.dumps(line), flush=True)

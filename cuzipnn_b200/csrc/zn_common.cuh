@@ -175,15 +175,16 @@ __device__ __forceinline__ void planes_to_elements(const uint32_t (*p)[4], uint3
 }
 
 // Loads and stores of 16-byte-element groups; `vec16` picks 16- or 8-byte transactions.
+// nwords is a compile-time constant at every call: the loops unroll fully, so w stays in registers.
 __device__ __forceinline__ void load_words(const uint8_t* p, uint32_t* w, int nwords, bool vec16) {
   if (vec16) {
-#pragma unroll 4
+#pragma unroll
     for (int i = 0; i < nwords; i += 4) {
       uint4 v = *reinterpret_cast<const uint4*>(p + 4 * i);
       w[i] = v.x; w[i + 1] = v.y; w[i + 2] = v.z; w[i + 3] = v.w;
     }
   } else {
-#pragma unroll 4
+#pragma unroll
     for (int i = 0; i < nwords; i += 2) {
       uint2 v = *reinterpret_cast<const uint2*>(p + 4 * i);
       w[i] = v.x; w[i + 1] = v.y;
@@ -193,10 +194,10 @@ __device__ __forceinline__ void load_words(const uint8_t* p, uint32_t* w, int nw
 
 __device__ __forceinline__ void store_words(uint8_t* p, const uint32_t* w, int nwords, bool vec16) {
   if (vec16) {
-#pragma unroll 4
+#pragma unroll
     for (int i = 0; i < nwords; i += 4) *reinterpret_cast<uint4*>(p + 4 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
   } else {
-#pragma unroll 4
+#pragma unroll
     for (int i = 0; i < nwords; i += 2) *reinterpret_cast<uint2*>(p + 4 * i) = make_uint2(w[i], w[i + 1]);
   }
 }

@@ -6,20 +6,32 @@
 // reg = I * x^(8L) mod P  xor  crc0(data), where crc0 is the register for initial value 0, and
 // zlib returns ~reg with I = 0xFFFFFFFF.  crc0 of a concatenation A|B is crc0(A) * x^(8|B|) xor
 // crc0(B), and leading zero bytes do not change crc0.  So each segment is right-aligned in a
-// virtual block of G equal pieces (zeros in front), every thread computes crc0 of its 128-byte
-// piece with slice-by-8 tables held in shared memory, multiplies it by x^(8 * 128 * (pieces after
-// it)) from a precomputed table, and an XOR reduction gives the block's crc0.  Segments longer
-// than one block (32 KiB) get one CTA per block and a second kernel combines the block values with
-// a binary tree of the constant multipliers x^(8 * 32 Ki * 2^k).
+// virtual block of G equal pieces of kPiece bytes (zeros in front); every thread computes crc0 of
+// its piece, multiplies it by x^(8 * kPiece * (pieces after it)) from a precomputed table, and an
+// XOR reduction gives the block's crc0.  Segments longer than one block (32 KiB) get one thread
+// group per block, and a second kernel combines the block values with a binary tree of the
+// constant multipliers x^(8 * 32 Ki * 2^k).  The term I * x^(8L) of a segment length L is
+// computed on the host.
+//
+// Lookups.  crc0 of a piece runs slice-by-4 (four 256-entry tables, one lookup per byte).  The
+// tables sit in shared memory replicated once per lane (128 KiB, one CTA per SM): lane l reads
+// only bank l, so a warp's 32 random lookups take one wavefront instead of ~3.5.  The address of
+// a lookup is one byte permute of the data word and the lane's column offset.  Data comes in
+// with 32-byte loads, the next 64 bytes in flight while the current ones are hashed; a CTA of 1024
+// threads (32 warps) hides the latency of the lookup chains.
 #include "zn_common.cuh"
 
 namespace zn {
 namespace {
 
-constexpr uint32_t kPoly = 0xEDB88320u;  // 0x04C11DB7 bit-reflected
-constexpr int kPiece = 128;              // bytes per thread
-constexpr int kThreads = 256;
-constexpr int64_t kBlock = int64_t(kPiece) * kThreads;  // 32 KiB
+constexpr uint32_t kPoly = 0xEDB88320u;                 // 0x04C11DB7 bit-reflected
+constexpr int kPiece = 512;                             // bytes per thread
+constexpr int kCrcThreads = 1024;                       // threads per CTA (64 registers each)
+constexpr int64_t kBlock = 32768;                       // bytes of one thread group of a long segment
+constexpr int kBlockThreads = int(kBlock / kPiece);     // 64: the largest group
+constexpr int kTableBytes = 4 * 256 * 32 * 4;           // slice-by-4 tables, one copy per lane
+constexpr int kCrcSmem = kTableBytes + kCrcThreads / 32 * 4;
+constexpr int kL2Threads = 256;                         // level 2: one CTA per segment
 
 // x^(8 * 2^i) mod P in the reflected representation (bit 31 is x^0), i = 0..63.
 struct PowTable {
@@ -44,11 +56,11 @@ constexpr PowTable make_pow_table() {
 
 __constant__ PowTable c_x8pow = make_pow_table();
 
-// Slice-by-8 tables (T[k][i]: the register after byte i followed by k zero bytes) and the piece
-// multipliers x^(8 * kPiece * m) mod P, m = 0 .. kThreads - 1, computed at compile time.
+// Slice-by-4 tables (t[k][i]: the register after byte i followed by k zero bytes) and the piece
+// multipliers x^(8 * kPiece * m) mod P, m < kBlockThreads, computed at compile time.
 struct CrcTables {
-  uint32_t t[8][256];
-  uint32_t piece_pow[256];
+  uint32_t t[4][256];
+  uint32_t piece_pow[kBlockThreads];
 };
 
 constexpr CrcTables make_crc_tables() {
@@ -60,15 +72,15 @@ constexpr CrcTables make_crc_tables() {
   }
   for (int i = 0; i < 256; ++i) {
     uint32_t c = r.t[0][i];
-    for (int k = 1; k < 8; ++k) {
+    for (int k = 1; k < 4; ++k) {
       c = (c >> 8) ^ r.t[0][c & 0xFF];
       r.t[k][i] = c;
     }
   }
-  const uint32_t x_piece = make_pow_table().v[7];  // x^(8 * 128)
-  static_assert(kPiece == 128, "piece_pow assumes 128-byte pieces");
-  r.piece_pow[0] = 0x80000000u;  // x^0
-  for (int m = 1; m < 256; ++m) r.piece_pow[m] = gf2_mul_c(r.piece_pow[m - 1], x_piece);
+  static_assert(kPiece == 512, "piece_pow uses x^(8 * 2^9)");
+  const uint32_t x_piece = make_pow_table().v[9];  // x^(8 * 512)
+  r.piece_pow[0] = 0x80000000u;                    // x^0
+  for (int m = 1; m < kBlockThreads; ++m) r.piece_pow[m] = gf2_mul_c(r.piece_pow[m - 1], x_piece);
   return r;
 }
 
@@ -92,50 +104,150 @@ __device__ uint32_t x8pow(uint64_t nbytes) {
   return r ? r : 0x80000000u;  // x^0 = 1
 }
 
-__device__ __forceinline__ uint32_t finish(uint32_t crc0, int64_t len) {
-  return ~(gf2_mul(0xFFFFFFFFu, x8pow(uint64_t(len))) ^ crc0);
+// The register term 0xFFFFFFFF * x^(8 L) mod P of a segment of L bytes (host): the CRC of the
+// segment is ~(term ^ crc0).
+uint32_t init_term(int64_t L) {
+  static const PowTable pw = make_pow_table();
+  uint32_t r = 0x80000000u;
+  for (int i = 0; L; ++i, L >>= 1)
+    if (L & 1) r = gf2_mul_c(r, pw.v[i]);
+  return gf2_mul_c(0xFFFFFFFFu, r);
 }
 
-// Slice-by-8 tables into shared memory, from the precomputed copy.
-__device__ void build_tables(uint32_t (*T)[256]) {
-  for (int i = threadIdx.x; i < 8 * 256; i += blockDim.x) T[i >> 8][i & 255] = g_crc_tables.t[i >> 8][i & 255];
+// ---- shared-memory tables, replicated per lane ------------------------------------------------
+// Entry t[k][b] for lane l at byte offset (k >> 1) << 16 | b << 8 | (k & 1) << 7 | l << 2: two
+// tables interleave in each 64 KiB half, and a lane's column is fixed, so its bank is l.
+
+__device__ void load_tables(uint8_t* T) {
+  for (int i = threadIdx.x; i < kTableBytes / 4; i += blockDim.x) {
+    const int k = i >> 13, b = (i >> 5) & 255, l = i & 31;
+    *reinterpret_cast<uint32_t*>(T + ((k >> 1) << 16 | b << 8 | (k & 1) << 7 | l << 2)) = g_crc_tables.t[k][b];
+  }
   __syncthreads();
 }
 
-__device__ __forceinline__ uint32_t crc_bytes(uint32_t c, const uint8_t* p, int64_t n, const uint32_t (*T)[256]) {
-  for (int64_t i = 0; i < n; ++i) c = T[0][(c ^ p[i]) & 0xFF] ^ (c >> 8);
+// t[K][byte POS of x] for the calling lane (lane4 = lane * 4): the byte permute builds
+// lane4 | byte << 8, the table's own offset is an immediate.
+template <int K, int POS>
+__device__ __forceinline__ uint32_t lut(const uint8_t* T, uint32_t x, uint32_t lane4) {
+  const uint32_t off = __byte_perm(x, lane4, 0x5504u | (POS << 4));
+  return *reinterpret_cast<const uint32_t*>(T + ((K >> 1) << 16) + ((K & 1) << 7) + off);
+}
+
+// Four bytes (the little-endian word w) into register c.
+__device__ __forceinline__ uint32_t step4(uint32_t c, uint32_t w, const uint8_t* T, uint32_t lane4) {
+  const uint32_t x = c ^ w;
+  return lut<3, 0>(T, x, lane4) ^ lut<2, 1>(T, x, lane4) ^ lut<1, 2>(T, x, lane4) ^ lut<0, 3>(T, x, lane4);
+}
+
+__device__ __forceinline__ uint32_t step1(uint32_t c, uint32_t byte, const uint8_t* T, uint32_t lane4) {
+  return lut<0, 0>(T, c ^ byte, lane4) ^ (c >> 8);
+}
+
+// 64 bytes from a 32-byte aligned address, as two 32-byte loads.
+__device__ __forceinline__ void ld64(const uint8_t* p, uint32_t (&w)[16]) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+    asm volatile("ld.global.nc.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(w[8 * q]), "=r"(w[8 * q + 1]), "=r"(w[8 * q + 2]), "=r"(w[8 * q + 3]), "=r"(w[8 * q + 4]),
+                   "=r"(w[8 * q + 5]), "=r"(w[8 * q + 6]), "=r"(w[8 * q + 7])
+                 : "l"(p + 32 * q));
+}
+
+// crc0 of the len bytes at p (any alignment): bytes up to the next 32-byte boundary, then 64-byte
+// chunks (the next chunk's loads issued before the current one is hashed), then 32-byte chunks,
+// words and bytes.
+__device__ __forceinline__ uint32_t crc_piece(const uint8_t* p, int len, const uint8_t* T, uint32_t lane4) {
+  uint32_t c = 0;
+  const int head = min(len, int((32 - (reinterpret_cast<uintptr_t>(p) & 31)) & 31));
+  for (int i = 0; i < head; ++i) c = step1(c, p[i], T, lane4);
+  p += head;
+  len -= head;
+  const int nch = len >> 6;
+  if (nch > 0) {
+    uint32_t A[16], B[16];
+    ld64(p, A);
+    for (int q = 0; q < nch; q += 2) {
+      if (q + 1 < nch) ld64(p + 64 * (q + 1), B);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) c = step4(c, A[i], T, lane4);
+      if (q + 1 >= nch) break;
+      if (q + 2 < nch) ld64(p + 64 * (q + 2), A);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) c = step4(c, B[i], T, lane4);
+    }
+    p += nch << 6;
+    len -= nch << 6;
+  }
+  for (; len >= 32; p += 32, len -= 32) {
+    uint32_t w[8];
+    asm volatile("ld.global.nc.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+                 : "l"(p));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c = step4(c, w[i], T, lane4);
+  }
+  for (; len >= 4; p += 4, len -= 4) c = step4(c, *reinterpret_cast<const uint32_t*>(p), T, lane4);
+  for (int i = 0; i < len; ++i) c = step1(c, p[i], T, lane4);
   return c;
 }
 
-__device__ __forceinline__ uint32_t crc_8(uint32_t c, uint32_t lo, uint32_t hi, const uint32_t (*T)[256]) {
-  lo ^= c;
-  return T[7][lo & 0xFF] ^ T[6][(lo >> 8) & 0xFF] ^ T[5][(lo >> 16) & 0xFF] ^ T[4][lo >> 24] ^
-         T[3][hi & 0xFF] ^ T[2][(hi >> 8) & 0xFF] ^ T[1][(hi >> 16) & 0xFF] ^ T[0][hi >> 24];
-}
-
-// crc0 of data[lo, hi) (hi - lo <= kPiece).
-__device__ __forceinline__ uint32_t crc_piece(const uint8_t* data, int64_t lo, int64_t hi, const uint32_t (*T)[256]) {
-  const uint8_t* p = data + lo;
-  if (hi - lo == kPiece && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+// Level 1: persistent CTAs (one per SM) over the work items, kCrcThreads / G groups of G threads
+// at a time.  single: an item is a segment of at most G * kPiece bytes, whose CRC the group writes
+// to out (init_full, init_last: the init terms of a full and of the last segment).  Otherwise an
+// item is a 32 KiB block of a long segment (G = kBlockThreads), whose crc0 goes to partial[].
+// The loop bound is the same for every thread of the CTA (the group reductions synchronise).
+__global__ void __launch_bounds__(kCrcThreads, 1) crc_pieces(const uint8_t* __restrict__ data, int64_t nbytes,
+                                                             int64_t seg, int64_t nseg, int G, int64_t bps,
+                                                             bool single, uint32_t init_full, uint32_t init_last,
+                                                             uint32_t* __restrict__ out, uint32_t* __restrict__ partial) {
+  extern __shared__ __align__(16) uint8_t T[];
+  uint32_t* red = reinterpret_cast<uint32_t*>(T + kTableBytes);
+  load_tables(T);
+  const int tid = threadIdx.x, lt = tid % G;
+  const uint32_t lane4 = uint32_t(tid & 31) << 2;
+  const int gpc = kCrcThreads / G;
+  const int64_t items = single ? nseg : nseg * bps;
+  // This thread's piece multiplier x^(8 * kPiece * (pieces after it in the group)).
+  const uint32_t mult = g_crc_tables.piece_pow[G - 1 - lt];
+  for (int64_t base = int64_t(blockIdx.x) * gpc; base < items; base += int64_t(gridDim.x) * gpc) {
+    const int64_t it = base + tid / G;
+    int64_t s = 0;
     uint32_t c = 0;
-#pragma unroll
-    for (int i = 0; i < kPiece; i += 16) {
-      const uint4 v = *reinterpret_cast<const uint4*>(p + i);
-      c = crc_8(c, v.x, v.y, T);
-      c = crc_8(c, v.z, v.w, T);
+    if (it < items) {
+      s = single ? it : it / bps;
+      const int64_t b = single ? 0 : it % bps;
+      const int64_t L = (s == nseg - 1) ? nbytes - s * seg : seg;
+      const int64_t nb = single ? 1 : cdiv(L, kBlock);
+      const int64_t pad = nb * int64_t(G) * kPiece - L;  // virtual leading zeros
+      const int64_t v0 = b * int64_t(G) * kPiece + int64_t(lt) * kPiece;
+      const int64_t lo = max(v0 - pad, int64_t(0)), hi = min(v0 + kPiece - pad, L);
+      if (hi > lo) c = crc_piece(data + s * seg + lo, int(hi - lo), T, lane4);
+      if (c && lt != G - 1) c = gf2_mul(c, mult);
     }
-    return c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1)
+      if (o < G) c ^= __shfl_xor_sync(0xFFFFFFFFu, c, o);
+    if (G > 32) {  // groups of whole warps: XOR the warps' values
+      if ((tid & 31) == 0) red[tid >> 5] = c;
+      __syncthreads();
+      if (lt == 0)
+        for (int w = 1; w < G / 32; ++w) c ^= red[(tid >> 5) + w];
+      __syncthreads();
+    }
+    if (lt == 0 && it < items) {
+      if (single) out[s] = ~((s == nseg - 1 ? init_last : init_full) ^ c);
+      else partial[it] = c;
+    }
   }
-  return hi > lo ? crc_bytes(0, p, hi - lo, T) : 0u;
 }
 
-// Tree-combine the crc0 values of G consecutive threads (G a power of two, <= blockDim.x) that
-// hold equal pieces of `piece_bytes` virtual bytes each; the group's crc0 ends in its first thread.
-// `mult` (shared, >= 9 entries) receives the per-level multipliers x^(8 * piece_bytes * 2^k).
-__device__ uint32_t combine_group(uint32_t c, int G, uint64_t piece_bytes, uint32_t* sm, uint32_t* mult) {
+// Tree-combine the crc0 values of the kL2Threads threads of a CTA that hold equal pieces of
+// `piece_bytes` virtual bytes each; the result ends in thread 0.
+__device__ uint32_t combine_group(uint32_t c, uint64_t piece_bytes, uint32_t* sm, uint32_t* mult) {
   const int t = threadIdx.x;
   int levels = 0;
-  while ((1 << levels) < G) ++levels;
+  while ((1 << levels) < kL2Threads) ++levels;
   if (t < levels) mult[t] = x8pow(piece_bytes << t);
   __syncthreads();
   for (int k = 0; k < levels; ++k) {
@@ -148,70 +260,20 @@ __device__ uint32_t combine_group(uint32_t c, int G, uint64_t piece_bytes, uint3
   return c;
 }
 
-// Level 1.  Segments of at most kBlock bytes: groups of G threads, one segment per group
-// (single_level), writing the final CRC.  Longer segments: one CTA per (segment, block) writing
-// the block's crc0 to partial[].
-__global__ void __launch_bounds__(kThreads) crc_level1(const uint8_t* __restrict__ data, int64_t nbytes, int64_t seg,
-                                                       int64_t nseg, int G, int64_t blocks_per_seg, bool single_level,
-                                                       uint32_t* __restrict__ out, uint32_t* __restrict__ partial) {
-  __shared__ uint32_t T[8][256];
-  __shared__ uint32_t sm[kThreads / 32];
-  build_tables(T);
-  const int t = threadIdx.x;
-  int64_t s, b;
-  int lt;  // thread index within its group
-  if (single_level) {
-    const int groups = kThreads / G;
-    s = int64_t(blockIdx.x) * groups + t / G;
-    b = 0;
-    lt = t % G;
-  } else {
-    s = blockIdx.x / blocks_per_seg;
-    b = blockIdx.x % blocks_per_seg;
-    lt = t;
-  }
-  uint32_t c = 0;
-  int64_t L = 0;
-  if (s < nseg) {
-    L = (s == nseg - 1) ? nbytes - s * seg : seg;
-    const int64_t nb = single_level ? 1 : cdiv(L, kBlock);
-    const int64_t vlen = nb * int64_t(G) * kPiece;  // virtual (right-aligned) segment length
-    const int64_t pad = vlen - L;
-    const int64_t v0 = b * int64_t(G) * kPiece + int64_t(lt) * kPiece;
-    const int64_t lo = max(v0 - pad, int64_t(0)), hi = min(v0 + kPiece - pad, L);
-    if (hi > lo) c = crc_piece(data + s * seg, lo, hi, T);
-  }
-  // The group's crc0 is the XOR over its pieces of crc0 * x^(8 * kPiece * (pieces after it)):
-  // one multiplication per thread by a precomputed power, then an XOR reduction.
-  if (c) c = gf2_mul(c, g_crc_tables.piece_pow[G - 1 - lt]);
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1)
-    if (o < G) c ^= __shfl_xor_sync(0xFFFFFFFFu, c, o);
-  if (G > 32) {  // groups of whole warps: XOR the warps' values
-    if ((t & 31) == 0) sm[t >> 5] = c;
-    __syncthreads();
-    if (lt == 0)
-      for (int w = 1; w < G / 32; ++w) c ^= sm[(t >> 5) + w];
-  }
-  if (lt == 0 && s < nseg) {
-    if (single_level) out[s] = finish(c, L);
-    else partial[s * blocks_per_seg + b] = c;
-  }
-}
-
 // Level 2: one CTA per segment combines its blocks' crc0 values (right-aligned like level 1).
-__global__ void __launch_bounds__(kThreads) crc_level2(int64_t nbytes, int64_t seg, int64_t nseg,
-                                                       int64_t blocks_per_seg, const uint32_t* __restrict__ partial,
-                                                       uint32_t* __restrict__ out) {
-  __shared__ uint32_t sm[kThreads];
+__global__ void __launch_bounds__(kL2Threads) crc_level2(int64_t nbytes, int64_t seg, int64_t nseg,
+                                                         int64_t blocks_per_seg, uint32_t init_full, uint32_t init_last,
+                                                         const uint32_t* __restrict__ partial,
+                                                         uint32_t* __restrict__ out) {
+  __shared__ uint32_t sm[kL2Threads];
   __shared__ uint32_t mult[16];
   __shared__ uint32_t step;
   const int64_t s = blockIdx.x;
   const int t = threadIdx.x;
   const int64_t L = (s == nseg - 1) ? nbytes - s * seg : seg;
   const int64_t nb = cdiv(L, kBlock);
-  const int64_t q = cdiv(nb, kThreads);  // blocks per thread
-  const int64_t shift = q * kThreads - nb;
+  const int64_t q = cdiv(nb, kL2Threads);  // blocks per thread
+  const int64_t shift = q * kL2Threads - nb;
   if (t == 0) step = x8pow(uint64_t(kBlock));
   __syncthreads();
   uint32_t h = 0;
@@ -220,8 +282,45 @@ __global__ void __launch_bounds__(kThreads) crc_level2(int64_t nbytes, int64_t s
     if (bi < 0) continue;  // leading virtual zero blocks
     h = (h ? gf2_mul(h, step) : 0u) ^ partial[s * blocks_per_seg + bi];
   }
-  h = combine_group(h, kThreads, uint64_t(q) * kBlock, sm, mult);
-  if (t == 0) out[s] = finish(h, L);
+  h = combine_group(h, uint64_t(q) * kBlock, sm, mult);
+  if (t == 0) out[s] = ~((s == nseg - 1 ? init_last : init_full) ^ h);
+}
+
+// Both levels for data[0, nbytes) in segments of segment_bytes.  partial: one u32 slot per
+// 32 KiB block of every segment longer than 32 KiB (crc_blocks), unused otherwise.
+int64_t crc_blocks(int64_t nbytes, int64_t segment_bytes) {
+  const int64_t seg = min(segment_bytes, nbytes);  // the longest segment
+  return seg > kBlock ? cdiv(nbytes, segment_bytes) * cdiv(seg, kBlock) : 0;
+}
+
+int launch_crc(const uint8_t* d, int64_t nbytes, int64_t segment_bytes, uint32_t* out, uint32_t* partial,
+               cudaStream_t st, const char* who) {
+  const int64_t nseg = cdiv(nbytes, segment_bytes);
+  const int64_t seg = min(segment_bytes, nbytes);
+  const int64_t bps = seg > kBlock ? cdiv(seg, kBlock) : 0;
+  int G = kBlockThreads;
+  if (bps == 0) {
+    G = 1;
+    while (int64_t(G) * kPiece < seg) G <<= 1;
+  }
+  const int64_t items = bps ? nseg * bps : nseg;
+  if (items > 0x7FFFFFFF || nseg > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "%s: too many segments", who);
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return set_error(ZN_ERR_CUDA, "%s: %s", who, cudaGetErrorString(e));
+  if (int rc = set_max_smem(reinterpret_cast<const void*>(crc_pieces), kCrcSmem)) return rc;
+  const int64_t grid = min(int64_t(sms), cdiv(items, int64_t(kCrcThreads / G)));
+  const uint32_t init_full = init_term(seg), init_last = init_term(nbytes - (nseg - 1) * segment_bytes);
+  {
+    TimedLaunch tl("crc", st);
+    crc_pieces<<<unsigned(grid), kCrcThreads, kCrcSmem, st>>>(d, nbytes, segment_bytes, nseg, G, bps, bps == 0,
+                                                              init_full, init_last, out, partial);
+    if (bps) crc_level2<<<unsigned(nseg), kL2Threads, 0, st>>>(nbytes, segment_bytes, nseg, bps, init_full, init_last,
+                                                              partial, out);
+  }
+  count_launch(bps ? 2 : 1);
+  return check_launch(who);
 }
 
 }  // namespace
@@ -233,50 +332,24 @@ extern "C" {
 
 size_t zn_crc32_temp_bytes(int64_t nbytes, int64_t segment_bytes) {
   if (nbytes <= 0 || segment_bytes <= 0) return 0;
-  const int64_t nseg = cdiv(nbytes, segment_bytes);
-  const int64_t seg = min(segment_bytes, nbytes);
-  if (seg <= kBlock) return 0;
-  return size_t(nseg * cdiv(seg, kBlock)) * sizeof(uint32_t);
+  return size_t(crc_blocks(nbytes, segment_bytes)) * sizeof(uint32_t);
 }
 
 int zn_crc32(const void* data, int64_t nbytes, int64_t segment_bytes, uint32_t* out, void* temp,
              size_t temp_bytes, void* stream) {
   if (nbytes < 0 || segment_bytes <= 0) return set_error(ZN_ERR_INVALID, "zn_crc32: bad arguments");
   if (nbytes == 0) return ZN_OK;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const uint8_t* d = static_cast<const uint8_t*>(data);
-  const int64_t nseg = cdiv(nbytes, segment_bytes);
-  const int64_t seg = min(segment_bytes, nbytes);  // longest segment
-  if (seg <= kBlock) {
-    int G = 1;
-    while (int64_t(G) * kPiece < seg) G <<= 1;
-    const int64_t groups = kThreads / G;
-    const int64_t grid = cdiv(nseg, groups);
-    if (grid > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_crc32: too many segments");
-    TimedLaunch tl("crc", st);
-    crc_level1<<<unsigned(grid), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, G, 1, true, out, nullptr);
-    count_launch();
-    return check_launch("zn_crc32");
-  }
-  const int64_t bps = cdiv(seg, kBlock);
-  if (temp_bytes < size_t(nseg * bps) * sizeof(uint32_t) || !temp)
+  const int64_t blocks = crc_blocks(nbytes, segment_bytes);
+  if (blocks && (!temp || temp_bytes < size_t(blocks) * sizeof(uint32_t)))
     return set_error(ZN_ERR_SPACE, "zn_crc32: temp buffer too small");
-  if (nseg * bps > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_crc32: too many blocks");
-  uint32_t* partial = static_cast<uint32_t*>(temp);
-  {
-    TimedLaunch tl("crc", st);  // both levels
-    crc_level1<<<unsigned(nseg * bps), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, kThreads, bps, false, out,
-                                                          partial);
-    crc_level2<<<unsigned(nseg), kThreads, 0, st>>>(nbytes, segment_bytes, nseg, bps, partial, out);
-  }
-  count_launch(2);
-  return check_launch("zn_crc32");
+  return launch_crc(static_cast<const uint8_t*>(data), nbytes, segment_bytes, out, static_cast<uint32_t*>(temp),
+                    static_cast<cudaStream_t>(stream), "zn_crc32");
 }
 
 }  // extern "C"
 
 // ---------------------------------------------------------------------------------------------
-// zn_crc32_noalloc: the same two kernels with their partial-CRC scratch in a static device array,
+// zn_crc32_noalloc: the same kernels with their partial-CRC scratch in a static device array,
 // for callers that must not allocate device memory (see the declaration in the public header).
 //
 // The array is 2 MiB: 524,288 u32 slots, one per 32 KiB block of every segment longer than
@@ -316,34 +389,15 @@ extern "C" int zn_crc32_noalloc(const void* data, int64_t nbytes, int64_t segmen
                                 void* stream) {
   if (nbytes < 0 || segment_bytes <= 0) return set_error(ZN_ERR_INVALID, "zn_crc32_noalloc: bad arguments");
   if (nbytes == 0) return ZN_OK;
-  const int64_t nseg = cdiv(nbytes, segment_bytes);
-  const int64_t seg = min(segment_bytes, nbytes);  // longest segment
-  const int64_t bps = seg > kBlock ? cdiv(seg, kBlock) : 0;
-  if (nseg * bps > kNoAllocSlots)
+  const int64_t slots = crc_blocks(nbytes, segment_bytes);
+  if (slots > kNoAllocSlots)
     return set_error(ZN_ERR_INVALID,
                      "zn_crc32_noalloc: %lld bytes in segments of %lld need %lld scratch slots (one per 32 KiB block "
                      "of each segment); the static scratch holds %lld (2 MiB). Use zn_crc32 with a temp buffer",
-                     (long long)nbytes, (long long)segment_bytes, (long long)(nseg * bps), (long long)kNoAllocSlots);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const uint8_t* d = static_cast<const uint8_t*>(data);
-  if (bps == 0) {  // every segment fits one CTA: the scratch is neither touched nor looked up
-    int G = 1;
-    while (int64_t(G) * kPiece < seg) G <<= 1;
-    const int64_t grid = cdiv(nseg, int64_t(kThreads / G));
-    if (grid > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_crc32_noalloc: too many segments");
-    TimedLaunch tl("crc", st);
-    crc_level1<<<unsigned(grid), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, G, 1, true, out, nullptr);
-    count_launch();
-    return check_launch("zn_crc32_noalloc");
-  }
-  uint32_t* partial = nullptr;
-  if (int rc = noalloc_scratch(&partial)) return rc;
-  {
-    TimedLaunch tl("crc", st);
-    crc_level1<<<unsigned(nseg * bps), kThreads, 0, st>>>(d, nbytes, segment_bytes, nseg, kThreads, bps, false, out,
-                                                          partial);
-    crc_level2<<<unsigned(nseg), kThreads, 0, st>>>(nbytes, segment_bytes, nseg, bps, partial, out);
-  }
-  count_launch(2);
-  return check_launch("zn_crc32_noalloc");
+                     (long long)nbytes, (long long)segment_bytes, (long long)slots, (long long)kNoAllocSlots);
+  uint32_t* partial = nullptr;  // segments of at most 32 KiB: the scratch is neither touched nor looked up
+  if (slots)
+    if (int rc = noalloc_scratch(&partial)) return rc;
+  return launch_crc(static_cast<const uint8_t*>(data), nbytes, segment_bytes, out, partial,
+                    static_cast<cudaStream_t>(stream), "zn_crc32_noalloc");
 }
