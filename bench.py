@@ -293,6 +293,7 @@ def main() -> None:
     ap.add_argument("--micro-only", action="store_true",
                     help="run only the seam and CRC micro-benchmarks and print their JSON")
     ap.add_argument("--no-micro", action="store_true")
+    ap.add_argument("--no-strong", action="store_true")
     ap.add_argument("--layers", type=int, default=None,
                     help="profile a smaller model: this many decoder layers, no embedding / LM head")
     args = ap.parse_args()
@@ -443,26 +444,35 @@ def main() -> None:
                   "path": "GPU tensor -> compress_tensor() defaults (CPU blob) -> decompress_tensor(blob, compute_device) "
                           "one tensor at a time, best of 2 passes, wall clock"}
 
-    # One model sharded over the ranks (whole tensors, plan_shards), strong scaling: device time of
-    # compress_shard + decompress_shard, max over ranks.
-    sharded = None
-    if world > 1:
-        ts = []
-        for s_i in range(3):
+    # Strong scaling: one copy of the model over the ranks (plan_model: tensors above half a rank's
+    # mean share split by chunk range, the rest whole, longest first): device time of
+    # compress_model_shard + decompress_model_shard, max over ranks, 3 warm-up + 5 timed passes.
+    strong = None
+    if not args.no_strong:
+        plan = z.plan_model([t.numel() * t.element_size() for t in model], world)  # once per model
+        tc_, td_ = [], []
+        for s_i in range(8):
             barrier()
             a = torch.cuda.Event(enable_timing=True)
+            m = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record()
-            loc = z.compress_shard(model, rank, world, readback_to_cpu=False)
-            back = z.decompress_shard(loc)
+            whole, parts = z.compress_model_shard(model, rank, world, plan=plan, readback_to_cpu=False)
+            m.record()
+            outs, pouts = z.decompress_model_shard(whole, parts)
             b.record()
             torch.cuda.synchronize()
-            if s_i:
-                ts.append(a.elapsed_time(b) / 1e3)
-            del loc, back
-        t_sh = max_over_ranks(sum(ts) / len(ts))
-        sharded = {"value": round(model_bytes / t_sh / GB, 3), "unit": "GB/s", "ms_per_step": round(t_sh * 1e3, 3),
-                   "scaling": "strong", "workload": "one copy of the model, whole tensors per rank (plan_shards)"}
+            if s_i >= 3:
+                tc_.append(a.elapsed_time(m) / 1e3)
+                td_.append(m.elapsed_time(b) / 1e3)
+            del whole, parts, outs, pouts
+        sc, sd = max_over_ranks(sum(tc_) / len(tc_)), max_over_ranks(sum(td_) / len(td_))
+        st = max_over_ranks(sum(c + d for c, d in zip(tc_, td_)) / len(tc_))
+        strong = {"value": round(model_bytes / st / GB, 3), "unit": "GB/s", "ms_per_step": round(st * 1e3, 3),
+                  "compress_gbs": round(model_bytes / sc / GB, 3), "decompress_gbs": round(model_bytes / sd / GB, 3),
+                  "scaling": "strong", "split_tensors": len(plan[1]),
+                  "workload": "one copy of the model over the ranks (plan_model: tensors above half a rank's "
+                              "share split by chunk range, the rest whole, longest first)"}
 
     # End to end through the public API from pinned host memory: H2D of the inputs, CPU blobs,
     # H2D of the blobs, and a D2H read of a result word each step.
@@ -534,7 +544,7 @@ def main() -> None:
             "cpu_baseline": cpu_baseline,
             "clocks": clocks.summary(),
             "e2e": e2e,
-            "sharded": sharded,
+            "strong": strong,
             "micro": micro,
             "gpu_launches": gpu_launches,
         }

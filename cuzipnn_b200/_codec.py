@@ -558,7 +558,18 @@ def _ptr_array(ctype, values):
 
 _PIPELINE_BYTES = 1 << 29  # sub-batch of host-resident inputs (upload overlapped with the kernels)
 _DEVICE_BATCH_BYTES = 1 << 32  # sub-batch of device-resident inputs (launched while the host prepares the next)
-_FIRST_BATCH_BYTES = 1 << 28  # the first sub-batch of a call is smaller, so that the GPU starts sooner
+# The first sub-batch of a call is small, so that the GPU starts soon: a sixteenth of the call's
+# bytes, between these bounds; each later one is _BATCH_GROWTH times larger (up to the batch
+# limit), so that the kernels of one batch run while the host prepares the next.
+_FIRST_BATCH_MIN = 1 << 25
+_FIRST_BATCH_MAX = 1 << 28
+_BATCH_GROWTH = 4
+
+
+def _batch_limit(limit: int, launched: int, total: int) -> int:
+    """Input bytes of the next sub-batch of a call of `total` bytes after `launched` sub-batches."""
+    first = min(max(total // 16, _FIRST_BATCH_MIN), _FIRST_BATCH_MAX)
+    return min(limit, first * _BATCH_GROWTH ** min(launched, 16))
 _TINY_BYTES = 65536  # stored tensors up to this size decode into views of one shared buffer per call
 _COPY_BATCH_MAX = 1 << 29  # largest single copy of one zn_copy_chunks launch (65535 tiles of 8 KiB)
 
@@ -712,6 +723,7 @@ def compress_tensors(
     # Coded tensors are launched in batches of one element size as the list is read (the first
     # batch smaller), so that the GPU starts while the host reads the rest.
     cur: dict[tuple[int, bool], tuple[list[int], int]] = {}
+    total = sum(t.numel() * t.element_size() for t in tensors)
     with contextlib.ExitStack() as ctx:
         for i, t in enumerate(tensors):
             if i == 0:  # the scalar arguments once, then each tensor's dtype and rank
@@ -732,7 +744,7 @@ def compress_tensors(
             key = (k, t.dtype in _REORDER)
             idx, nbytes = cur.get(key, ([], 0))
             limit = _DEVICE_BATCH_BYTES if t.is_cuda else _PIPELINE_BYTES
-            if idx and nbytes + n * k > (limit if pending else min(limit, _FIRST_BATCH_BYTES)):
+            if idx and nbytes + n * k > _batch_limit(limit, len(pending), total):
                 launch(key[0], key[1], idx)
                 idx, nbytes = [], 0
             idx.append(i)
@@ -916,10 +928,13 @@ def decompress_tensors(
     stream = copy_in = status = None
     uploaded: list[torch.cuda.Event] = []
     pos = 0
+    launched = 0  # sub-batches launched so far
     cur: dict[tuple[int, bool], tuple[list, int]] = {}
+    total = sum(b.numel() for b in blobs)
 
     def launch(k: int, reorder: bool, items: list) -> None:
-        nonlocal copy_in, pos
+        nonlocal copy_in, pos, launched
+        launched += 1
         host = any(not blobs[i].is_cuda for i, _ in items)
         if host and copy_in is None:
             copy_in = _side_stream(device, 0)
@@ -997,7 +1012,7 @@ def decompress_tensors(
         items.append((i, (dtype, shape, chunk_bytes, n_comp, n)))
         nbytes += blob.numel()
         limit = _PIPELINE_BYTES if not blob.is_cuda else _DEVICE_BATCH_BYTES
-        if nbytes >= (min(limit, _FIRST_BATCH_BYTES) if pos == 0 else limit):
+        if nbytes >= _batch_limit(limit, launched, total):
             with torch.cuda.device(device):
                 launch(key[0], key[1], items)
             items, nbytes = [], 0

@@ -15,6 +15,7 @@ decompress_chunk_range go the other way.
 
 from __future__ import annotations
 
+import heapq
 import math
 import struct
 from collections.abc import Sequence
@@ -143,6 +144,90 @@ def compress_chunk_range(
     part = tensor.detach().reshape(-1)[j0 * chunk_bytes : min(j1 * chunk_bytes, n)]
     # min_compress_bytes = 0: the part is coded like the whole tensor even when it is small.
     return compress_tensor(part, min_compress_bytes=0, **kw)
+
+
+# ---- a whole model over several GPUs: large tensors by chunk range, the rest whole -------------
+
+
+def plan_model(nbytes: Sequence[int], world: int, split_bytes: int | None = None) -> tuple[list[list[int]], list[int]]:
+    """Plan a model's tensors (byte sizes `nbytes`) over `world` ranks for strong scaling.  Tensors
+    of more than split_bytes bytes (default: half a rank's mean share, sum / (2 * world)) are split:
+    every rank compresses its chunk range of each (plan_chunk_ranges), so they add about 1 / world
+    of their bytes to every rank.  The other tensors go whole to ranks, longest first, each to the
+    rank with the fewest bytes so far (ties: lowest rank).  Deterministic.
+
+    Returns (whole, split): whole[r] = indices of the tensors rank r takes whole (ascending),
+    split = indices of the split tensors (ascending)."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    total = sum(int(b) for b in nbytes)
+    if split_bytes is None:
+        split_bytes = total // (2 * world)
+    sizes = [int(b) for b in nbytes]
+    split = [i for i, b in enumerate(sizes) if world > 1 and b > split_bytes]
+    share = sum(sizes[i] for i in split) // world
+    heap = [(share, r) for r in range(world)]  # (load, rank): the least-loaded, lowest rank first
+    whole: list[list[int]] = [[] for _ in range(world)]
+    cut = set(split)
+    for i in sorted((i for i in range(len(sizes)) if i not in cut), key=lambda i: (-sizes[i], i)):
+        load, r = heapq.heappop(heap)
+        whole[r].append(i)
+        heapq.heappush(heap, (load + sizes[i], r))
+    for w in whole:
+        w.sort()
+    return whole, split
+
+
+def _range_part(tensor: torch.Tensor, rank: int, world: int, chunk_bytes: int) -> torch.Tensor:
+    """The flat elements of this rank's chunk range of a tensor (plan_chunk_ranges)."""
+    n = tensor.numel()
+    j0, j1 = plan_chunk_ranges(n, chunk_bytes, world)[rank]
+    return tensor.detach().reshape(-1)[j0 * chunk_bytes : min(j1 * chunk_bytes, n)]
+
+
+def compress_model_shard(
+    tensors: Sequence[torch.Tensor], rank: int, world: int, *, split_bytes: int | None = None,
+    plan: tuple[list[list[int]], list[int]] | None = None, **kwargs
+) -> tuple[dict[int, torch.Tensor], dict[int, torch.Tensor]]:
+    """This rank's share of a model (plan_model) compressed on the current device: returns (whole,
+    parts), whole = {tensor index: blob} of the tensors it takes whole, parts = {tensor index: this
+    rank's chunk-range part} of the split tensors (compress_chunk_range's blob; gather_chunk_ranges
+    and assemble_chunk_ranges join the parts of all ranks into the tensor's blob).  One
+    compress_tensors call covers the whole tensors and every part that is coded anyway; keyword
+    arguments are compress_tensors'.  `plan`, if given, is plan_model's result for these tensors and
+    this world (a loader plans a model once), else it is computed here."""
+    if not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    whole_idx, split = plan if plan is not None else plan_model([_nbytes(t) for t in tensors], world, split_bytes)
+    chunk = kwargs.get("chunk_bytes", C.DEFAULT_CHUNK_BYTES)
+    minb = kwargs.get("min_compress_bytes", C.DEFAULT_MIN_COMPRESS_BYTES)
+    items, keys, parts = [tensors[i] for i in whole_idx[rank]], list(whole_idx[rank]), {}
+    part_keys = []
+    for i in split:
+        t = tensors[i]
+        if _nbytes(t) < minb or t.numel() == 0:  # the stored or the empty path: rank 0 holds it whole
+            if rank == 0:
+                parts[i] = compress_chunk_range(t, rank, world, **kwargs)
+            continue
+        part = _range_part(t, rank, world, chunk)
+        if part.numel() * part.element_size() >= minb:
+            items.append(part)
+            part_keys.append(i)
+        else:  # a short (or empty) range is coded with min_compress_bytes = 0, as compress_chunk_range does
+            parts[i] = compress_chunk_range(t, rank, world, **kwargs)
+    blobs = compress_tensors(items, **kwargs) if items else []
+    whole = dict(zip(keys, blobs[: len(keys)]))
+    parts.update(zip(part_keys, blobs[len(keys) :]))
+    return whole, parts
+
+
+def decompress_model_shard(whole: dict[int, torch.Tensor], parts: dict[int, torch.Tensor], **kwargs
+                           ) -> tuple[dict[int, torch.Tensor], dict[int, torch.Tensor]]:
+    """Decompress what compress_model_shard returned, in one decompress_tensors call: (tensors by
+    index, this rank's flat elements of each split tensor by index)."""
+    wk, pk = sorted(whole), sorted(parts)
+    outs = decompress_tensors([whole[i] for i in wk] + [parts[i] for i in pk], **kwargs) if wk or pk else []
+    return dict(zip(wk, outs[: len(wk)])), {i: o.reshape(-1) for i, o in zip(pk, outs[len(wk) :])}
 
 
 class _Tables:

@@ -2,6 +2,7 @@
 // for large dynamic shared memory, NVTX ranges and the opt-in kernel timing.
 #include <nvtx3/nvToolsExt.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -111,23 +112,42 @@ int zn_timing_enable(const char* kernel, int enable) {
 
 int zn_timing_read(const char* kernel, double* total_ms, int64_t* launches) {
   std::lock_guard<std::mutex> lock(zn::g_timing.mu);
-  double sum = 0;
-  int64_t count = 0;
+  // Launches of one kind may overlap (the Python layer runs a call's sub-batches on two streams),
+  // so the time is the union of their [start, stop] intervals, measured from the kind's first
+  // start event: the time during which at least one of them ran.
+  std::vector<std::pair<double, double>> iv;
   std::vector<zn::Timing::Rec> keep;
+  cudaEvent_t origin = nullptr;
   for (auto& r : zn::g_timing.pending) {
     if (kernel && r.kernel != kernel) {
       keep.push_back(r);
       continue;
     }
-    float ms = 0;
-    if (cudaEventSynchronize(r.stop) != cudaSuccess || cudaEventElapsedTime(&ms, r.start, r.stop) != cudaSuccess)
+    float a = 0, b = 0;
+    if (cudaEventSynchronize(r.stop) != cudaSuccess)
       return zn::set_error(ZN_ERR_CUDA, "zn_timing_read: %s", cudaGetErrorString(cudaGetLastError()));
-    sum += ms;
-    ++count;
+    if (!origin) origin = r.start;
+    if (cudaEventElapsedTime(&a, origin, r.start) != cudaSuccess || cudaEventElapsedTime(&b, origin, r.stop) != cudaSuccess)
+      return zn::set_error(ZN_ERR_CUDA, "zn_timing_read: %s", cudaGetErrorString(cudaGetLastError()));
+    iv.push_back({double(a), double(b)});
     zn::g_timing.pool.push_back({r.start, r.stop});
   }
   zn::g_timing.pending.swap(keep);
-  if (launches) *launches = count;
+  std::sort(iv.begin(), iv.end());
+  double sum = 0, lo = 0, hi = 0;
+  bool open = false;
+  for (auto& x : iv) {
+    if (!open || x.first > hi) {
+      if (open) sum += hi - lo;
+      lo = x.first;
+      hi = x.second;
+      open = true;
+    } else if (x.second > hi) {
+      hi = x.second;
+    }
+  }
+  if (open) sum += hi - lo;
+  if (launches) *launches = int64_t(iv.size());
   if (total_ms) *total_ms = sum;
   return ZN_OK;
 }

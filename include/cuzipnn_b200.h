@@ -46,8 +46,9 @@ uint64_t zn_launch_count(void);
 /* Kernel timing for measurement (no reference counterpart): while enabled, every launch of the
  * named kernel kind ("hist", "encode", "scan", "pack", "dscan", "decode", "decode_overflow",
  * "crc", or "*" for all) is bracketed by CUDA events on its launching stream.  zn_timing_read
- * waits for the recorded events of one kind (NULL: all) and returns their summed duration and
- * count, then forgets them. */
+ * waits for the recorded events of one kind (NULL: all) and returns the launches' count and the
+ * time during which at least one of them ran (the union of their intervals: their summed duration
+ * when they do not overlap), then forgets them. */
 int zn_timing_enable(const char *kernel, int enable);
 int zn_timing_read(const char *kernel, double *total_ms, int64_t *launches);
 

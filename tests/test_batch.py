@@ -123,3 +123,30 @@ def test_device_inputs_in_sub_batches(monkeypatch):
     assert z.last_decode_status() == 0
     for t, y in zip(ts, outs):
         assert torch.equal(bits(y.cpu()), bits(t.cpu()))
+
+
+def test_many_sub_batches_keep_stream_order(monkeypatch):
+    """A call split into many sub-batches (the first one small, each later one larger) on a
+    non-default stream: inputs written in place on that stream just before the call and results
+    read on it just after (no synchronization in between) round-trip exactly."""
+    from cuzipnn_b200 import _codec
+
+    monkeypatch.setattr(_codec, "_FIRST_BATCH_MIN", 1 << 16)
+    monkeypatch.setattr(_codec, "_FIRST_BATCH_MAX", 1 << 16)
+    monkeypatch.setattr(_codec, "_DEVICE_BATCH_BYTES", 1 << 20)
+    g = torch.Generator(device="cuda").manual_seed(8)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        xs = [torch.randn(n, generator=g, device="cuda").to(torch.bfloat16) for n in (300_000, 200_001, 500_000, 90_000)]
+        refs = [x.clone() for x in xs]
+        for x in xs:
+            x.mul_(0.02)  # in place, on s, right before the call
+        blobs = z.compress_tensors(xs, readback_to_cpu=False)
+        outs = z.decompress_tensors(blobs)
+        ok = [torch.equal(o.view(torch.int16), (r * 0.02).view(torch.int16)) for o, r in zip(outs, refs)]
+        for x in xs:
+            x.zero_()  # the inputs are free for reuse once the call returns
+    torch.cuda.synchronize()
+    assert all(ok)
+    assert z.last_decode_status() == 0

@@ -47,6 +47,27 @@ def test_plan_shards_is_lpt_and_deterministic():
         z.plan_shards(sizes, 0)
 
 
+def test_plan_model_splits_large_tensors_and_balances_the_rest():
+    sizes = [1090, 1090] + [136] * 84 + [25] * 56 + [4] * 56 + [0, 3]
+    for world in (1, 2, 3, 4, 8, 16):
+        whole, split = z.plan_model(sizes, world)
+        assert (whole, split) == z.plan_model(sizes, world)
+        seen = sorted([i for w in whole for i in w] + split)
+        assert seen == list(range(len(sizes)))
+        assert all(sizes[i] > sum(sizes) // (2 * world) for i in split)
+        if world == 1:
+            assert split == []
+        share = sum(sizes[i] for i in split) // world
+        loads = [share + sum(sizes[i] for i in w) for w in whole]
+        rest = [sizes[i] for i in range(len(sizes)) if i not in split]
+        assert max(loads) <= sum(sizes) / world + max(rest), world
+    assert z.plan_model(sizes, 8)[1] == [0, 1]
+    assert z.plan_model(sizes, 2)[1] == []  # 1090 < half of a rank's share
+    assert z.plan_model(sizes, 2, split_bytes=1000)[1] == [0, 1]
+    with pytest.raises(ValueError):
+        z.plan_model(sizes, 0)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
