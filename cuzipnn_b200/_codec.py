@@ -262,7 +262,10 @@ def hash_tensor_with_crc32(
     x = tensor.detach()
     device = _gpu(x, _check_device(compute_device))
     with torch.cuda.device(device):
-        x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+        if x.is_cuda:
+            x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+        else:
+            x = _upload(x.contiguous(), device)
         crc = _crc32(x.view(-1).view(torch.uint8), checksum_chunk_bytes)
         return crc.cpu() if readback_to_cpu else crc
 
@@ -349,7 +352,9 @@ def _compress(
 
     device = _gpu(x, compute_device)
     with _on(device):
-        if not (x.device == device and x.is_contiguous()):
+        if not x.is_cuda:
+            x = _upload(x.contiguous(), device)
+        elif not (x.device == device and x.is_contiguous()):
             x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
         x = x.view(-1)
         if x.data_ptr() % 16:
@@ -377,9 +382,13 @@ def _compress(
         if not readback_to_cpu:
             return _remember(comp, tensor.dtype, tuple(tensor.shape), _FLAG_REORDER if reorder else 0, chunk_bytes,
                              n), crc
-        blob = _populated_empty(size, pin_memory=pin_memory)
-        # With a crc, crc.cpu() below syncs the stream, so blob is complete on return.
-        blob.copy_(comp, non_blocking=crc is not None)
+        if pin_memory:
+            blob = _populated_empty(size, pin_memory=True)
+            # With a crc, crc.cpu() below syncs the stream, so blob is complete on return.
+            blob.copy_(comp, non_blocking=crc is not None)
+        else:
+            blob = _host_empty(size)
+            _download(comp, blob)
         return blob, None if crc is None else crc.cpu()
 
 
@@ -518,7 +527,9 @@ def decompress_tensor(
 
     with _on(device):
         x = blob
-        if not (x.device == device and x.is_contiguous()):
+        if not x.is_cuda:
+            x = _upload(x.contiguous(), device)
+        elif not (x.device == device and x.is_contiguous()):
             x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
         if x.data_ptr() % 8:
             x = x.clone()
@@ -544,8 +555,8 @@ def decompress_tensor(
         if readback_to_cpu:
             src = y
             y = host_out if host_out is not None else (
-                _populated_empty(src.numel() * src.element_size()).view(src.dtype).view_as(src))
-            y.copy_(src)
+                _host_empty(src.numel() * src.element_size()).view(src.dtype).view_as(src))
+            _download(src, y)
             if int(status.item()):
                 raise ValueError(f"blob is corrupt (decoder status {int(status.item())})")
 
@@ -698,7 +709,11 @@ def compress_tensors(
             xs = []
             for i in idx:
                 x = tensors[i].detach()
-                if not (x.device == device and x.is_contiguous() and x.data_ptr() % 16 == 0):
+                if not x.is_cuda:
+                    x = _upload(x.contiguous(), device)
+                    if x.data_ptr() % 16:
+                        x = x.clone()
+                elif not (x.device == device and x.is_contiguous() and x.data_ptr() % 16 == 0):
                     x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
                     if x.data_ptr() % 16:
                         x = x.clone()
@@ -792,8 +807,12 @@ def compress_tensors(
             copy_out.wait_event(done)
             with torch.cuda.stream(copy_out):
                 for j, (i, o, size) in enumerate(zip(idx, offs, sizes_b)):
-                    blob = hbuf[hoffs[j] : hoffs[j] + size] if pin_memory else _populated_empty(size)
-                    blob.copy_(out[o : o + size], non_blocking=pin_memory)
+                    if pin_memory:
+                        blob = hbuf[hoffs[j] : hoffs[j] + size]
+                        blob.copy_(out[o : o + size], non_blocking=True)
+                    else:
+                        blob = _host_empty(size)
+                        _download(out[o : o + size], blob)
                     blobs[i] = blob
             out.record_stream(copy_out)  # its memory returns to the allocator after the downloads
             entry[1] = out = None
@@ -943,7 +962,11 @@ def decompress_tensors(
             xs = []
             for i, _ in items:
                 x = blobs[i]
-                if not (x.device == device and x.is_contiguous() and x.data_ptr() % 8 == 0):
+                if not x.is_cuda:
+                    x = _upload(x.contiguous(), device)
+                    if x.data_ptr() % 8:
+                        x = x.clone()
+                elif not (x.device == device and x.is_contiguous() and x.data_ptr() % 8 == 0):
                     x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
                     if x.data_ptr() % 8:
                         x = x.clone()
@@ -1032,8 +1055,8 @@ def decompress_tensors(
             for i, y in enumerate(outs):
                 if y is not None and y.is_cuda:
                     host = dest[i] if dest[i] is not None else (
-                        _populated_empty(y.numel() * y.element_size()).view(y.dtype).view_as(y))
-                    host.copy_(y)
+                        _host_empty(y.numel() * y.element_size()).view(y.dtype).view_as(y))
+                    _download(y, host)
                     outs[i] = host
     return outs  # type: ignore[return-value]
 
@@ -1056,6 +1079,78 @@ def _gather_prefixes(device: torch.device, bs: list[torch.Tensor], plen: list[in
             offs.append(pos)
             pos += p
         return flat, offs
+
+
+# Host copies between the GPU and pageable memory of at least _BOUNCE_MIN bytes run through two
+# pinned bounce buffers of _BOUNCE_BYTES (per thread and device): the DMA of one piece overlaps the
+# host copy of the previous one (PyTorch spreads a large host copy over its CPU threads, which also
+# fault the destination's fresh pages in parallel).  A plain copy to or from pageable memory is
+# staged by the driver one piece at a time on one thread.
+_BOUNCE_BYTES = 1 << 25
+_BOUNCE_MIN = 1 << 23
+_BOUNCE = threading.local()
+
+
+def _bounce(device: torch.device) -> tuple[list[torch.Tensor], list[torch.cuda.Event]]:
+    cache = getattr(_BOUNCE, "by_dev", None)
+    if cache is None:
+        cache = _BOUNCE.by_dev = {}
+    b = cache.get(device.index)
+    if b is None:
+        b = cache[device.index] = ([torch.empty(_BOUNCE_BYTES, dtype=torch.uint8, pin_memory=True) for _ in range(2)],
+                                   [torch.cuda.Event(), torch.cuda.Event()])
+    return b
+
+
+def _host_empty(size: int) -> torch.Tensor:
+    """A pageable host buffer for a download: fresh pages for a bounced copy (which faults them in
+    on many threads), pre-faulted ones for a plain copy."""
+    return torch.empty(size, dtype=torch.uint8) if size >= _BOUNCE_MIN else _populated_empty(size)
+
+
+def _download(src: torch.Tensor, dst: torch.Tensor) -> None:
+    """Copy contiguous GPU tensor `src` into contiguous host tensor `dst` (same byte size) on the
+    current stream; returns once dst holds the data."""
+    s8, d8 = src.reshape(-1).view(torch.uint8), dst.reshape(-1).view(torch.uint8)
+    n = s8.numel()
+    if n < _BOUNCE_MIN or dst.is_pinned():
+        d8.copy_(s8)
+        return
+    bufs, evs = _bounce(src.device)
+    stream = torch.cuda.current_stream(src.device)
+    prev = None
+    for i, off in enumerate(range(0, n, _BOUNCE_BYTES)):
+        j, m = i % 2, min(_BOUNCE_BYTES, n - off)
+        evs[j].synchronize()  # the buffer's previous use (an upload of this thread) is done
+        bufs[j][:m].copy_(s8[off : off + m], non_blocking=True)
+        evs[j].record(stream)
+        if prev is not None:
+            pj, poff, pm = prev
+            evs[pj].synchronize()
+            d8[poff : poff + pm].copy_(bufs[pj][:pm])
+        prev = (j, off, m)
+    pj, poff, pm = prev
+    evs[pj].synchronize()
+    d8[poff : poff + pm].copy_(bufs[pj][:pm])
+
+
+def _upload(src: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """A copy on `device` of contiguous host tensor `src`, enqueued on the current stream; src may
+    be reused once this returns."""
+    n = src.numel() * src.element_size()
+    if n < _BOUNCE_MIN or src.is_pinned():
+        return src.to(device, non_blocking=True)
+    dst = torch.empty(src.shape, dtype=src.dtype, device=device)
+    s8, d8 = src.reshape(-1).view(torch.uint8), dst.reshape(-1).view(torch.uint8)
+    bufs, evs = _bounce(device)
+    stream = torch.cuda.current_stream(device)
+    for i, off in enumerate(range(0, n, _BOUNCE_BYTES)):
+        j, m = i % 2, min(_BOUNCE_BYTES, n - off)
+        evs[j].synchronize()  # the DMA that last read this buffer is done
+        bufs[j][:m].copy_(s8[off : off + m])
+        d8[off : off + m].copy_(bufs[j][:m], non_blocking=True)
+        evs[j].record(stream)
+    return dst
 
 
 def _populated_empty(size: int, *, pin_memory: bool = False) -> torch.Tensor:

@@ -150,3 +150,25 @@ def test_many_sub_batches_keep_stream_order(monkeypatch):
     torch.cuda.synchronize()
     assert all(ok)
     assert z.last_decode_status() == 0
+
+
+def test_large_pageable_host_copies():
+    """Host blobs and host tensors above the bounce threshold (copies through the pinned bounce
+    buffers, in pieces that do not divide the size) round-trip exactly, per tensor and batched,
+    with the pinned path unchanged."""
+    g = torch.Generator().manual_seed(12)
+    x = (torch.randn(70 * 1024 * 1024 // 4 + 3, generator=g) * 0.02)  # ~70 MiB fp32 on the host
+    y = (torch.randn(9_000_001, generator=g) * 0.02).to(torch.bfloat16)
+    blob = z.compress_tensor(x)  # host input, host blob
+    assert not blob.is_cuda and not blob.is_pinned()
+    assert torch.equal(blob, z.compress_tensor(x.cuda(), pin_memory=True))
+    back = z.decompress_tensor(blob, compute_device="cuda")
+    assert torch.equal(back.cpu(), x)
+    assert torch.equal(z.decompress_tensor(blob, compute_device="cuda", readback_to_cpu=True), x)
+    blobs = z.compress_tensors([x, y, x[:1000]])
+    assert torch.equal(blobs[0], blob)
+    outs = z.decompress_tensors(blobs, readback_to_cpu=True)
+    assert torch.equal(outs[0], x) and torch.equal(outs[1].view(torch.int16), y.view(torch.int16))
+    assert torch.equal(outs[2], x[:1000])
+    h = z.hash_tensor_with_crc32(x, checksum_chunk_bytes=1 << 20)
+    assert torch.equal(h, z.hash_tensor_with_crc32(x.cuda(), checksum_chunk_bytes=1 << 20))
