@@ -574,7 +574,7 @@ _DEVICE_BATCH_BYTES = 1 << 32  # sub-batch of device-resident inputs (launched w
 # limit), so that the kernels of one batch run while the host prepares the next.
 _FIRST_BATCH_MIN = 1 << 25
 _FIRST_BATCH_MAX = 1 << 28
-_BATCH_GROWTH = 4
+_BATCH_GROWTH = 16
 
 
 def _batch_limit(limit: int, launched: int, total: int) -> int:
