@@ -5,25 +5,23 @@ reference (ruihe774/cuZipNN, src/cuzipnn/_codec.py) and replaces its GPU pipelin
 nvCOMP ANS, a blocking host-side passthrough decision, table upload and two copy passes) with one
 call into libcuzipnn_b200.so per direction.
 
-Blob layout (little-endian, every section 8-byte aligned), as in src/cuzipnn/_codec.py:3-20:
+The container (src/cuzipnn/_codec.py:3-20), little-endian, with every section starting on an
+8-byte boundary:
 
-    0   magic "ZNNG" | u8 version | u8 dtype code | u8 ndim | u8 flags
-    8   u32 chunk_bytes | u32 n_comp
-    16  u64 numel
-    24  i64 shape[ndim]
+    bytes 0-3    "ZNNG"             byte 4   version (3 here)     byte 5   dtype code
+    byte 6       ndim               byte 7   flags: 1 = exponent bits reordered, 2 = stored raw
+    bytes 8-11   chunk_bytes        bytes 12-15  n_comp           bytes 16-23  numel
+    then         ndim int64 dimensions
 
-flags: bit 0 = exponent bit reordering, bit 1 = stored uncompressed.
+A tensor below min_compress_bytes is "stored": chunk_bytes and n_comp are 0 and its bytes follow
+the header as they are.  Any other tensor has K byte streams (K = element size) cut into
+nch = ceil(numel / chunk_bytes) chunks, and after the header come: an int32 per (stream, chunk)
+unit with the bytes it occupies, an int32 per rANS-coded unit with its index (ascending), padding
+to 8, and the units themselves in (stream, chunk) order, each padded to 8 bytes.
 
-A stored blob (tensors smaller than min_compress_bytes) has chunk_bytes = n_comp = 0, and the
-header is followed directly by the tensor's bytes in row-major order.  Otherwise it continues:
-
-    ..  i32 stored_bytes[K * nch]  bytes stored for each (stream, chunk), rANS-coded or raw
-    ..  i32 comp_idx[n_comp]       indices of the rANS-coded chunks
-    ..  data                       chunks in (stream, chunk) order, each padded to 8 bytes
-
-The version byte is 3: coded chunks hold ZNR2 rANS payloads (see include/cuzipnn_b200.h), not
-nvCOMP ANS streams, so version-2 blobs of the reference are rejected, as the reference rejects
-other versions (src/cuzipnn/_codec.py:423-424).
+Version 3 marks coded units as ZNR2 rANS payloads (include/cuzipnn_b200.h), not nvCOMP ANS
+streams; version-2 blobs of the reference are therefore rejected, as the reference rejects
+versions other than its own (src/cuzipnn/_codec.py:423-424).
 """
 
 from __future__ import annotations
@@ -93,31 +91,33 @@ def _sub_chunks(chunk_bytes: int, sub_chunk_bytes: int) -> int:
 
 
 def _layout(ndim: int, total: int, n_comp: int) -> tuple[int, int, int]:
-    """Offsets of the stored_bytes table, the comp_idx table and the data (_codec.py:89-93)."""
-    sizes_off = 24 + 8 * ndim
-    idx_off = sizes_off + 4 * total
-    data_off = _align8(idx_off + 4 * n_comp)
-    return sizes_off, idx_off, data_off
+    """Where the unit-size table, the coded-index table and the unit data start in a blob with
+    `total` units of which n_comp are coded (the container of _codec.py:89-93)."""
+    head = _FIXED.size + 8 * ndim
+    return head, head + 4 * total, _align8(head + 4 * (total + n_comp))
 
 
 def _check_device(compute_device: torch.device | str | None) -> torch.device | None:
-    """Validate compute_device without initializing CUDA (_codec.py:96-103)."""
+    """Parse compute_device and insist on a CUDA device (the rule of _codec.py:96-103).  No CUDA
+    call is made, so a bad value is reported the same way on a machine without a GPU."""
     if compute_device is None:
         return None
-    device = torch.device(compute_device)
-    if device.type != "cuda":
-        raise ValueError(f"compute_device must be a CUDA device, not {device}")
-    return device
+    dev = compute_device if isinstance(compute_device, torch.device) else torch.device(compute_device)
+    if dev.type == "cuda":
+        return dev
+    raise ValueError(f"compute_device must be a CUDA device, not {dev}")
 
 
 def _gpu(x: torch.Tensor, compute_device: torch.device | None) -> torch.device:
-    """compute_device if given, else x's device if it is on the GPU, else the current CUDA device."""
-    device = compute_device
-    if device is None:
-        device = x.device if x.is_cuda else torch.device("cuda")
-    if device.index is None:
-        device = torch.device("cuda", torch.cuda.current_device())
-    return device
+    """The GPU a call works on, with an explicit index: the device the caller named, else the
+    tensor's own GPU, else the current CUDA device (the rule of _codec.py:106-113)."""
+    if compute_device is not None:
+        dev = compute_device
+    elif x.is_cuda:
+        dev = x.device
+    else:
+        dev = torch.device("cuda")
+    return dev if dev.index is not None else torch.device("cuda", torch.cuda.current_device())
 
 
 def _stream(device: torch.device) -> int:
@@ -173,17 +173,22 @@ def _crc32(data: torch.Tensor, checksum_chunk_bytes: int) -> torch.Tensor:
 def _fill_stored(
     blob: torch.Tensor, offset: int, x: torch.Tensor, checksum_chunk_bytes: int | None
 ) -> tuple[torch.Tensor, torch.Tensor | None]:
-    """Copy x's bytes into blob[offset:], after the header.  With checksum_chunk_bytes the blob
-    is hashed on the CPU with zlib, as the reference does for these small blobs (_codec.py:134-147)."""
+    """Write the tensor's bytes behind the header of a host blob (blob[offset:]) and, when
+    checksums are asked for, hash the finished blob segment by segment with zlib on the host: a
+    blob this small costs less to hash there than to send to the GPU and back (the stored path of
+    _codec.py:134-147)."""
     blob[offset:].view(x.dtype).view(x.shape).copy_(x)
     if checksum_chunk_bytes is None:
         return blob, None
-    data = memoryview((ctypes.c_char * blob.numel()).from_address(blob.data_ptr()))
-    crc = [
-        zlib.crc32(data[i : i + checksum_chunk_bytes])
-        for i in range(0, len(data), checksum_chunk_bytes)
-    ]
-    return blob, torch.tensor(crc, dtype=torch.uint32)
+    return blob, _host_crc32(blob, checksum_chunk_bytes)
+
+
+def _host_crc32(blob: torch.Tensor, checksum_chunk_bytes: int) -> torch.Tensor:
+    """zlib CRC-32 of each checksum_chunk_bytes-byte segment of a host uint8 tensor (the last one
+    possibly shorter), as a uint32 tensor."""
+    raw = memoryview(blob.numpy())
+    starts = range(0, len(raw), checksum_chunk_bytes)
+    return torch.tensor([zlib.crc32(raw[i : i + checksum_chunk_bytes]) for i in starts], dtype=torch.uint32)
 
 
 def compress_tensor(

@@ -130,6 +130,8 @@ def compress_chunk_range(
 
     A tensor that takes the stored or the empty path has no chunks: rank 0 returns its whole blob
     and the other ranks None.  assemble_chunk_ranges joins the parts into the whole tensor's blob.
+    Parts carry no checksums (a CRC segment of the whole blob spans parts): ask
+    assemble_chunk_ranges for them (checksum_chunk_bytes), which hashes the assembled blob.
     """
     if not 0 <= rank < world:
         raise ValueError("rank must be in [0, world)")
@@ -286,12 +288,27 @@ def _prefix(dtype, shape, flags, chunk_bytes, numel, stored: np.ndarray, idx: np
 
 
 def assemble_chunk_ranges(
-    parts: Sequence[torch.Tensor | None], shape: Sequence[int], *, device: torch.device | str | None = None
-) -> torch.Tensor:
+    parts: Sequence[torch.Tensor | None], shape: Sequence[int], *, device: torch.device | str | None = None,
+    checksum_chunk_bytes: int | None = None,
+) -> torch.Tensor | tuple[torch.Tensor, torch.Tensor]:
     """The blob of the whole tensor (shape `shape`) from the parts compress_chunk_range made, in
     rank order; byte for byte the blob compress_tensor makes of the whole tensor with the same
     arguments.  The blob is placed on `device` (default: the first part's device); parts on other
-    devices are copied from there.  Raises ValueError if the parts do not fit together."""
+    devices are copied from there.  Raises ValueError if the parts do not fit together.
+
+    With checksum_chunk_bytes, returns (blob, crc) instead, crc as compress_tensor_with_crc32
+    gives it for the whole tensor (hash_tensor_with_crc32 of the assembled blob)."""
+    blob = _assemble(parts, shape, device)
+    if checksum_chunk_bytes is None:
+        return blob
+    if checksum_chunk_bytes <= 0:
+        raise ValueError("checksum_chunk_bytes must be positive")
+    if blob.is_cuda:
+        return blob, C.hash_tensor_with_crc32(blob, checksum_chunk_bytes=checksum_chunk_bytes, readback_to_cpu=False)
+    return blob, C._host_crc32(blob, checksum_chunk_bytes)
+
+
+def _assemble(parts: Sequence[torch.Tensor | None], shape: Sequence[int], device) -> torch.Tensor:
     shape = tuple(int(s) for s in shape)
     live = [p for p in parts if p is not None]
     if not live:

@@ -155,3 +155,15 @@ def test_gather_on_one_rank_gloo():
     assert [p.exitcode for p in procs] == [0, 0, 0, 0]
     x = _tensor(torch.bfloat16, 2 * C + 9, seed=4)
     assert np.array_equal(np.load(os.path.join(outdir, "blob.npy")), _blob(x, (2 * C + 9,), min_compress_bytes=0).numpy())
+
+
+def test_assembled_blob_checksums_equal_whole_tensor_crc():
+    """assemble_chunk_ranges(..., checksum_chunk_bytes) gives compress_tensor_with_crc32's CRCs of
+    the whole tensor (host blobs: the stored path, hashed with zlib)."""
+    x = torch.randn(300, 7)
+    parts = [z.compress_chunk_range(x, r, 3) for r in range(3)]
+    blob, crc = z.assemble_chunk_ranges(parts, x.shape, checksum_chunk_bytes=100)
+    ref_blob, ref_crc = z.compress_tensor_with_crc32(x, checksum_chunk_bytes=100)
+    assert torch.equal(blob, ref_blob) and torch.equal(crc, ref_crc)
+    with pytest.raises(ValueError):
+        z.assemble_chunk_ranges(parts, x.shape, checksum_chunk_bytes=0)

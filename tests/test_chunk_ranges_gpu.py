@@ -114,3 +114,13 @@ def test_two_gpu_ranges_gathered_over_nccl():
     assert [p.exitcode for p in procs] == [0, 0]
     ref = z.compress_tensor(_big().cuda(), readback_to_cpu=True)
     assert np.array_equal(np.load(os.path.join(outdir, "blob.npy")), ref.numpy())
+
+
+def test_assembled_blob_checksums_on_gpu():
+    """CRCs of an assembled coded blob equal compress_tensor_with_crc32's for the whole tensor."""
+    g = torch.Generator(device="cuda").manual_seed(6)
+    x = (torch.randn(1_000_003, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    parts = [z.compress_chunk_range(x, r, 4, readback_to_cpu=False) for r in range(4)]
+    blob, crc = z.assemble_chunk_ranges(parts, x.shape, checksum_chunk_bytes=16384)
+    ref_blob, ref_crc = z.compress_tensor_with_crc32(x, checksum_chunk_bytes=16384, readback_to_cpu=False)
+    assert torch.equal(blob, ref_blob) and torch.equal(crc, ref_crc)
