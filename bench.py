@@ -10,7 +10,11 @@ A step compresses every tensor (compress_tensors, blobs kept on the GPU) and dec
 blob (decompress_tensors): value = original bytes of all GPUs / step time, in GB/s (1e9).  The
 inputs (15 GB) are far larger than the 126 MB L2, so no flush is needed between steps.  With
 torchrun each rank processes its own copy of the model (weak scaling); times are the max over
-ranks.
+ranks.  The line also reports, measured after the timed steps: `strong` (one copy of the model
+over the ranks, plan_model), one tensor at a time on the device, the reference README's own
+methodology (GPU tensor -> CPU blob -> GPU, one tensor at a time, best of two passes, wall clock),
+`e2e` from pinned host tensors, `micro` (the byte-plane seams and CRC-32 on 1 GiB), the CPU
+baseline and the SM clocks seen during the timed region.
 
 --impl reference times the reference's CPU arm: the repository's C restatement of the codec path
 (oracle/, the checker), on all host cores, on a bounded sample of the same workload.
