@@ -2,18 +2,21 @@
 // (zn_ans_compress).
 //
 // zn_compress replaces src/cuzipnn/_codec.py:308-413 (split, nvCOMP ANS, host passthrough
-// decision and table build, two copy passes, prefix upload) with three kernels and no host round
+// decision and table build, two copy passes, prefix upload) with four kernels and no host round
 // trip:
-//   1. encode_kernel: one CTA per chunk.  It streams the chunk's elements once to build the
-//      histograms of all K byte planes (shared-memory atomics, 16 lane-private columns), turns
-//      each into a ZNR2 frequency table, and rANS-encodes every plane that can still come out
-//      below the passthrough budget into a scratch slot.  A plane whose entropy lower bound is
-//      already at or above the budget is skipped (it would be stored raw anyway).
-//   2. scan_kernel: one CTA applies the passthrough rule of _codec.py:361-372, writes the header,
-//      the stored_bytes and comp_idx tables, and the destination of every unit.
-//   3. pack_kernel: one CTA per chunk re-reads the chunk (in reverse order, so the most recently
-//      encoded chunks are still in L2), writes raw planes straight from the elements and copies
-//      the coded payloads from scratch, zero-padding every unit to 8 bytes.
+//   1. hist_kernel: one CTA per chunk counts the byte histograms of all K planes of its elements
+//      (shared-memory atomics into lane-private columns) and writes one histogram per plane.
+//   2. encode_kernel: one CTA per chunk turns each plane's histogram into a ZNR2 frequency table,
+//      skips the planes whose entropy lower bound already fails the passthrough budget (they would
+//      be stored raw anyway), rANS-encodes the others into a scratch slot per unit, and writes the
+//      skipped (raw) planes straight to the blob offsets they have when every chunk codes the same
+//      planes.
+//   3. scan_kernel: one CTA per tensor applies the passthrough rule of _codec.py:361-372, writes
+//      the header, the stored_bytes and comp_idx tables and the destination of every unit, and
+//      checks the encoder's guessed raw-plane offsets against the final layout.
+//   4. pack_kernel: one CTA per chunk copies the coded payloads from scratch into the blob, writes
+//      the raw planes the encoder did not place (re-reading those elements), and zero-pads every
+//      unit to 8 bytes.
 #include <climits>
 #include <type_traits>
 #include <math.h>
