@@ -28,6 +28,7 @@ from __future__ import annotations
 
 import contextlib
 import ctypes
+import functools
 import math
 import struct
 import threading
@@ -310,10 +311,14 @@ def _check_args(
 
 def _header(tensor: torch.Tensor, flags: int, chunk_bytes: int, n_comp: int) -> bytes:
     """The fixed header and shape (_codec.py:270-292)."""
-    fixed = _FIXED.pack(
-        _MAGIC, _VERSION, _CODES[tensor.dtype], tensor.dim(), flags, chunk_bytes, n_comp, tensor.numel()
-    )
-    return fixed + struct.pack(f"<{tensor.dim()}q", *tensor.shape)
+    return _header_bytes(tensor.dtype, tuple(tensor.shape), flags, chunk_bytes, n_comp)
+
+
+@functools.lru_cache(maxsize=4096)
+def _header_bytes(dtype: torch.dtype, shape: tuple[int, ...], flags: int, chunk_bytes: int, n_comp: int) -> bytes:
+    """Header bytes by their fields: a model's tensors share few shapes, so most are packed once."""
+    fixed = _FIXED.pack(_MAGIC, _VERSION, _CODES[dtype], len(shape), flags, chunk_bytes, n_comp, math.prod(shape))
+    return fixed + struct.pack(f"<{len(shape)}q", *shape)
 
 
 def _compress(
@@ -617,27 +622,33 @@ def _copy_batch(device: torch.device, srcs: list[int], dsts: list[int], sizes: l
     )
 
 
-def _stored_blobs_gpu(items: list[tuple[int, torch.Tensor, bytes]], device: torch.device) -> dict[int, torch.Tensor]:
+def _stored_blobs_gpu(items: list[tuple[int, torch.Tensor, bytes, tuple]], device: torch.device) -> dict[int, torch.Tensor]:
     """Blobs of the stored path (header + raw bytes) for many tensors, built on the GPU by one
-    header upload and one batched copy.  Each blob is a view into one shared buffer."""
-    offs, pos = [], 0
-    for _, x, head in items:
+    header upload and one batched copy.  items: (index, tensor, header, header fields for
+    _remember).  Each blob is a view into one shared buffer (256-byte aligned), all made by one
+    split of it."""
+    dev = device.index
+    nbs = [x.numel() * x.element_size() for _, x, _, _ in items]
+    pieces, offs, pos = [], [], 0
+    for (_, _, head, _), nb in zip(items, nbs):
+        size = len(head) + nb
+        step = (size + 255) & ~255
         offs.append(pos)
-        pos += (len(head) + x.numel() * x.element_size() + 255) & ~255
-    out = torch.empty(max(pos, 1), dtype=torch.uint8, device=device)
-    heads = b"".join(h for _, _, h in items)
-    hdev = torch.frombuffer(bytearray(heads), dtype=torch.uint8).pin_memory().to(device, non_blocking=True)
+        pieces += (size, step - size)
+        pos += step
+    out = torch.empty(pos, dtype=torch.uint8, device=device)
+    hdev = torch.frombuffer(bytearray(b"".join(h for _, _, h, _ in items)), dtype=torch.uint8).pin_memory()
+    hdev = hdev.to(device, non_blocking=True)
     srcs, dsts, sizes = [], [], []
     hpos, hbase, obase = 0, hdev.data_ptr(), out.data_ptr()
-    for (_, x, head), o in zip(items, offs):
+    for (_, x, head, _), o, nb in zip(items, offs, nbs):
         hl = len(head)
         srcs.append(hbase + hpos)
         dsts.append(obase + o)
         sizes.append(hl)
         hpos += hl
-        nb = x.numel() * x.element_size()
         if nb:
-            if not (x.device == device and x.is_contiguous() and x.data_ptr() % 8 == 0):
+            if not (x.is_cuda and x.get_device() == dev and x.is_contiguous() and x.data_ptr() % 8 == 0):
                 x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
                 if x.data_ptr() % 8:
                     x = x.clone()
@@ -647,7 +658,8 @@ def _stored_blobs_gpu(items: list[tuple[int, torch.Tensor, bytes]], device: torc
     # `hdev` and the staged inputs were allocated on this stream, so the caching allocator reuses
     # their memory only after the copy has run.
     _copy_batch(device, srcs, dsts, sizes)
-    return {i: out[o : o + len(head) + x.numel() * x.element_size()] for (i, x, head), o in zip(items, offs)}
+    views = out.split(pieces)
+    return {i: _remember(views[2 * j], *fields) for j, (i, _, _, fields) in enumerate(items)}
 
 
 def compress_tensors(
@@ -682,10 +694,11 @@ def compress_tensors(
             t = tensors[i]
             k, n = t.element_size(), t.numel()
             if (device is not None and not readback_to_cpu and n * k <= _COPY_BATCH_MAX
-                    and (t.device == device if cd is None and t.is_cuda else _gpu(t, cd) == device)):
+                    and (t.get_device() == device.index if cd is None and t.is_cuda else _gpu(t, cd) == device)):
                 stored = n * k < min_compress_bytes
                 flags = _FLAG_STORED if stored else _FLAG_REORDER if t.dtype in _REORDER else 0
-                batch.append((i, t.detach(), _header(t, flags, 0 if stored else chunk_bytes, 0)))
+                cbf = 0 if stored else chunk_bytes
+                batch.append((i, t.detach(), _header(t, flags, cbf, 0), (t.dtype, tuple(t.shape), flags, cbf, n)))
             else:
                 blobs[i] = compress_tensor(t, chunk_bytes=chunk_bytes, sub_chunk_bytes=sub_chunk_bytes,
                                            passthrough_threshold=passthrough_threshold,
@@ -693,10 +706,7 @@ def compress_tensors(
                                            compute_device=compute_device, readback_to_cpu=readback_to_cpu)
         if batch:
             for i, b in _stored_blobs_gpu(batch, device).items():
-                t = tensors[i]
-                stored = t.numel() * t.element_size() < min_compress_bytes
-                flags = _FLAG_STORED if stored else _FLAG_REORDER if t.dtype in _REORDER else 0
-                blobs[i] = _remember(b, t.dtype, tuple(t.shape), flags, 0 if stored else chunk_bytes, t.numel())
+                blobs[i] = b
 
     device: torch.device | None = None
     stream = copy_in = None
@@ -712,17 +722,18 @@ def compress_tensors(
         up = copy_in if host else stream
         with torch.cuda.stream(up):
             xs = []
+            dev = device.index
             for i in idx:
-                x = tensors[i].detach()
+                x = tensors[i]
                 if not x.is_cuda:
-                    x = _upload(x.contiguous(), device)
+                    x = _upload(x.detach().contiguous(), device)
                     if x.data_ptr() % 16:
                         x = x.clone()
-                elif not (x.device == device and x.is_contiguous() and x.data_ptr() % 16 == 0):
-                    x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+                elif not (x.get_device() == dev and x.is_contiguous() and x.data_ptr() % 16 == 0):
+                    x = x.detach().to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
                     if x.data_ptr() % 16:
                         x = x.clone()
-                xs.append(x.view(-1))
+                xs.append(x)  # only its address and size are used
         if up is not stream:
             stream.wait_stream(up)
             for x in xs:
@@ -831,25 +842,33 @@ def _launch_compress_batch(device, xs, srcs, k, reorder, chunk_bytes, sub_chunks
     """zn_compress_batch for device tensors `xs` (flat, 16-byte aligned; `srcs` the original
     tensors, for the headers) on the current stream: one blob buffer holding every blob at
     offs[j] (capacity zn_compress_bound each) and a device int64 size per blob."""
-    heads, caps, offs = [], [], []
+    flags = _FLAG_REORDER if reorder else 0
+    heads, caps, offs, ns = [], [], [], []
     total_cap = 0
     for x, t in zip(xs, srcs):
-        heads.append(_header(t, _FLAG_REORDER if reorder else 0, chunk_bytes, 0))
-        cap = int(_lib.lib.zn_compress_bound(x.numel(), k, t.dim(), chunk_bytes))
+        heads.append(_header(t, flags, chunk_bytes, 0))
+        n = x.numel()
+        ns.append(n)
+        cap = int(_lib.lib.zn_compress_bound(n, k, t.dim(), chunk_bytes))
         caps.append(cap)
         offs.append(total_cap)
         total_cap += (cap + 255) & ~255
     out = torch.empty(total_cap, dtype=torch.uint8, device=device)
     nj = len(xs)
     sizes = torch.empty(nj, dtype=torch.int64, device=device)
-    n_arr = _ptr_array(ctypes.c_int64, [x.numel() for x in xs])
+    n_arr = _ptr_array(ctypes.c_int64, ns)
     tb = int(_lib.lib.zn_compress_batch_temp_bytes(nj, n_arr, k, chunk_bytes, sub_chunks))
     temp = torch.empty(max(tb, 1), dtype=torch.uint8, device=device)
-    hbufs = [ctypes.create_string_buffer(h, len(h)) for h in heads]
+    # Every header in one host buffer; the library copies them into its job table during the call.
+    hbuf = ctypes.create_string_buffer(b"".join(heads))
+    hptrs, hpos = [], ctypes.addressof(hbuf)
+    for h in heads:
+        hptrs.append(hpos)
+        hpos += len(h)
     _lib.check(
         _lib.lib.zn_compress_batch(
             nj, _ptr_array(ctypes.c_void_p, [x.data_ptr() for x in xs]), n_arr, k, int(reorder),
-            _ptr_array(ctypes.c_void_p, [ctypes.addressof(h) for h in hbufs]),
+            _ptr_array(ctypes.c_void_p, hptrs),
             _ptr_array(ctypes.c_int, [len(h) for h in heads]), chunk_bytes, sub_chunks, float(threshold),
             _ptr_array(ctypes.c_void_p, [out.data_ptr() + o for o in offs]),
             _ptr_array(ctypes.c_int64, caps), sizes.data_ptr(), temp.data_ptr(), tb, _stream(device),
@@ -908,42 +927,51 @@ def decompress_tensors(
         """Stored blobs on the GPU decode into GPU tensors by one batched copy; the rest (CPU blobs,
         CPU outputs, empty tensors) take decompress_tensor."""
         srcs, dsts, sizes, tiny = [], [], [], []
-        bdev = None  # the one device whose stored blobs are batched
+        bdev = None  # the one device (index) whose stored blobs are batched
+        if compute_device is None:
+            cdi = None
+        else:
+            cdi = compute_device.index if compute_device.index is not None else torch.cuda.current_device()
         for i, dtype, shape, flags in small:
             b = blobs[i]
             header_size = _FIXED.size + 8 * len(shape)
             nbytes = math.prod(shape) * dtype.itemsize
-            if (flags & _FLAG_STORED and b.is_cuda and not readback_to_cpu and 0 < nbytes <= _COPY_BATCH_MAX
-                    and (b.data_ptr() + header_size) % 8 == 0
-                    and (compute_device is None or _gpu(b, compute_device) == b.device)
-                    and (dest[i] is None or (dest[i].device == b.device and dest[i].data_ptr() % 8 == 0))
-                    and bdev in (None, b.device)):
-                bdev = b.device
+            bi = b.get_device() if b.is_cuda else None
+            d = dest[i]
+            if (flags & _FLAG_STORED and bi is not None and not readback_to_cpu and 0 < nbytes <= _COPY_BATCH_MAX
+                    and (b.data_ptr() + header_size) % 8 == 0 and cdi in (None, bi) and bdev in (None, bi)
+                    and (d is None or (d.is_cuda and d.get_device() == bi and d.data_ptr() % 8 == 0))):
+                bdev = bi
                 if b.numel() < header_size + nbytes:
                     raise ValueError("blob is truncated")
                 srcs.append(b.data_ptr() + header_size)
                 sizes.append(nbytes)
-                if dest[i] is None and nbytes <= _TINY_BYTES:  # placed in one shared buffer below
+                if d is None and nbytes <= _TINY_BYTES:  # placed in one shared buffer below
                     tiny.append((i, dtype, shape, nbytes, len(dsts)))
                     dsts.append(0)
                 else:
-                    y = torch.empty(shape, dtype=dtype, device=b.device) if dest[i] is None else dest[i]
+                    y = torch.empty(shape, dtype=dtype, device=b.device) if d is None else d
                     dsts.append(y.data_ptr())
                     outs[i] = y
             else:
                 outs[i] = decompress_tensor(b, compute_device=compute_device, readback_to_cpu=readback_to_cpu,
-                                            out=dest[i])
+                                            out=d)
         if srcs:
+            dev = torch.device("cuda", bdev)
             if tiny:
-                total = sum((nb + 255) & ~255 for _, _, _, nb, _ in tiny)
-                buf = torch.empty(total, dtype=torch.uint8, device=bdev)
-                pos = 0
-                for i, dtype, shape, nb, j in tiny:
-                    outs[i] = buf[pos : pos + nb].view(dtype).view(shape)
-                    dsts[j] = buf.data_ptr() + pos
+                pieces, pos = [], 0
+                for _, _, _, nb, j in tiny:
+                    step = (nb + 255) & ~255
+                    pieces += (nb, step - nb)
+                    pos += step
+                buf = torch.empty(pos, dtype=torch.uint8, device=dev)
+                views, base, pos = buf.split(pieces), buf.data_ptr(), 0
+                for q, (i, dtype, shape, nb, j) in enumerate(tiny):
+                    outs[i] = views[2 * q].view(dtype).view(shape)
+                    dsts[j] = base + pos
                     pos += (nb + 255) & ~255
-            with torch.cuda.device(bdev):
-                _copy_batch(bdev, srcs, dsts, sizes)
+            with torch.cuda.device(dev):
+                _copy_batch(dev, srcs, dsts, sizes)
 
     # Coded blobs are launched in batches as they are parsed, so that the GPU starts on the first
     # batch while the host prepares the next.  Host-resident blobs go up on a copy stream in
@@ -965,13 +993,14 @@ def decompress_tensors(
         up = copy_in if host else stream
         with torch.cuda.stream(up):
             xs = []
+            dev = device.index
             for i, _ in items:
                 x = blobs[i]
                 if not x.is_cuda:
                     x = _upload(x.contiguous(), device)
                     if x.data_ptr() % 8:
                         x = x.clone()
-                elif not (x.device == device and x.is_contiguous() and x.data_ptr() % 8 == 0):
+                elif not (x.get_device() == dev and x.is_contiguous() and x.data_ptr() % 8 == 0):
                     x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
                     if x.data_ptr() % 8:
                         x = x.clone()
