@@ -310,3 +310,38 @@ def test_device_read_n_comp_with_truncated_blob(z):
             assert torch.equal(out.view(torch.int16), x.view(torch.int16))
         else:
             assert int((out.view(torch.int16) != 0).sum()) == 0
+
+
+@pytest.mark.parametrize("k,reorder", [(1, False), (2, True), (2, False), (4, True), (8, False)])
+@pytest.mark.parametrize("xoff,poff,pad", [(0, 0, 0), (8, 0, 0), (0, 8, 8), (0, 3, 5), (-1, 0, 0)])
+def test_split_merge_alignment_paths(k, reorder, xoff, poff, pad):
+    """zn_split / zn_merge through the C ABI for every vector path: elements 16- or 8-byte aligned,
+    or element-aligned only (xoff = -1: offset by one element, the scalar kernels); plane starts
+    16-, 8- or 1-byte aligned (planar offset and stride); merge chunks not a multiple of 16 (groups
+    that straddle chunks) and sources off 8-byte alignment.  Equal to the oracle byte for byte."""
+    from cuzipnn_b200 import _lib
+
+    n = 100_003
+    xoff = k if xoff < 0 else xoff
+    stride = n + pad
+    g = torch.Generator().manual_seed(k * 31 + xoff + poff)
+    raw = torch.randint(0, 256, (n * k,), generator=g, dtype=torch.uint8)
+    s = torch.cuda.current_stream().cuda_stream
+    xbuf = torch.zeros(n * k + 64, dtype=torch.uint8, device="cuda")
+    xbuf[xoff : xoff + n * k].copy_(raw)
+    pbuf = torch.zeros(k * stride + 64, dtype=torch.uint8, device="cuda")
+    assert _lib.lib.zn_split(xbuf.data_ptr() + xoff, n, k, int(reorder), pbuf.data_ptr() + poff, stride, s) == 0
+    ref = O.split(raw.numpy(), n, k, reorder, stride)
+    assert np.array_equal(pbuf[poff : poff + k * stride].cpu().numpy(), ref)
+    # Merge back from planes laid out with chunks of C elements (C a multiple of 8, not of 16 when
+    # 1000), read through a base that is 8-byte aligned or not.
+    for C, boff in ((1024, 0), (1000, 0), (1024, 3)):
+        nch = -(-n // C)
+        planes = O.split(raw.numpy(), n, k, reorder, nch * C)  # k planes of stride nch * C
+        base = torch.zeros(planes.size + 64, dtype=torch.uint8, device="cuda")
+        base[boff : boff + planes.size].copy_(torch.from_numpy(planes))
+        tbl = torch.tensor([b * nch * C + j * C for b in range(k) for j in range(nch)], dtype=torch.int64, device="cuda")
+        obuf = torch.zeros(n * k + 64, dtype=torch.uint8, device="cuda")
+        rc = _lib.lib.zn_merge(tbl.data_ptr(), base.data_ptr() + boff, obuf.data_ptr() + xoff, n, k, C, int(reorder), s)
+        assert rc == 0
+        assert np.array_equal(obuf[xoff : xoff + n * k].cpu().numpy(), raw.numpy()), (C, boff)
