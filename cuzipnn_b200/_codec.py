@@ -144,6 +144,26 @@ def _remember(blob: torch.Tensor, dtype: torch.dtype, shape: tuple[int, ...], fl
     return blob
 
 
+def _remember_views(out: torch.Tensor, sizes: list[int], offs: list[int], fields: list[tuple]) -> list[torch.Tensor]:
+    """Blobs of one batch buffer: the view out[offs[j] : offs[j] + sizes[j]] of each, made by one
+    split, each remembering fields[j] = (dtype, shape, flags, chunk_bytes, n) as _remember does.
+    Views share the buffer's version counter, and each view's address and size follow from the
+    offsets, so no view is asked for them."""
+    pieces = []
+    end = out.numel()
+    for j, o in enumerate(offs):
+        nxt = offs[j + 1] if j + 1 < len(offs) else end
+        pieces += (sizes[j], nxt - o - sizes[j])
+    views = out.split(pieces)
+    ver, base = out._version, out.data_ptr()
+    blobs = []
+    for j, f in enumerate(fields):
+        v = views[2 * j]
+        v._zn_header = (ver, base + offs[j], sizes[j]) + f
+        blobs.append(v)
+    return blobs
+
+
 def _known_header(blob: torch.Tensor):
     """(dtype, shape, flags, chunk_bytes, n) of a GPU blob from _remember, if it still applies."""
     h = getattr(blob, "_zn_header", None)
@@ -579,18 +599,20 @@ def _ptr_array(ctype, values):
 
 _PIPELINE_BYTES = 1 << 29  # sub-batch of host-resident inputs (upload overlapped with the kernels)
 _DEVICE_BATCH_BYTES = 1 << 32  # sub-batch of device-resident inputs (launched while the host prepares the next)
-# The first sub-batch of a call is small, so that the GPU starts soon: a sixteenth of the call's
-# bytes, between these bounds; each later one is _BATCH_GROWTH times larger (up to the batch
-# limit), so that the kernels of one batch run while the host prepares the next.
-_FIRST_BATCH_MIN = 1 << 25
-_FIRST_BATCH_MAX = 1 << 28
+# The first sub-batch of a call is launched once _FIRST_BATCH bytes are read, so that the GPU
+# starts soon; each later one is _BATCH_GROWTH times larger (up to the batch limit), so that the
+# kernels of one batch run while the host prepares the next.  256 MB keep the kernels of the first
+# batch busy (~0.2 ms) for as long as the host needs to read and launch the next few hundred
+# tensors, without a pass over the whole list before the first launch.
+_FIRST_BATCH = 1 << 28
 _BATCH_GROWTH = 16
 
 
-def _batch_limit(limit: int, launched: int, total: int) -> int:
-    """Input bytes of the next sub-batch of a call of `total` bytes after `launched` sub-batches."""
-    first = min(max(total // 16, _FIRST_BATCH_MIN), _FIRST_BATCH_MAX)
-    return min(limit, first * _BATCH_GROWTH ** min(launched, 16))
+def _batch_limit(limit: int, launched: int) -> int:
+    """Input bytes of the next sub-batch of a call after `launched` sub-batches."""
+    return min(limit, _FIRST_BATCH * _BATCH_GROWTH ** min(launched, 16))
+
+
 _TINY_BYTES = 65536  # stored tensors up to this size decode into views of one shared buffer per call
 _COPY_BATCH_MAX = 1 << 29  # largest single copy of one zn_copy_chunks launch (65535 tiles of 8 KiB)
 
@@ -629,13 +651,10 @@ def _stored_blobs_gpu(items: list[tuple[int, torch.Tensor, bytes, tuple]], devic
     split of it."""
     dev = device.index
     nbs = [x.numel() * x.element_size() for _, x, _, _ in items]
-    pieces, offs, pos = [], [], 0
+    offs, pos = [], 0
     for (_, _, head, _), nb in zip(items, nbs):
-        size = len(head) + nb
-        step = (size + 255) & ~255
         offs.append(pos)
-        pieces += (size, step - size)
-        pos += step
+        pos += (len(head) + nb + 255) & ~255
     out = torch.empty(pos, dtype=torch.uint8, device=device)
     hdev = torch.frombuffer(bytearray(b"".join(h for _, _, h, _ in items)), dtype=torch.uint8).pin_memory()
     hdev = hdev.to(device, non_blocking=True)
@@ -658,8 +677,9 @@ def _stored_blobs_gpu(items: list[tuple[int, torch.Tensor, bytes, tuple]], devic
     # `hdev` and the staged inputs were allocated on this stream, so the caching allocator reuses
     # their memory only after the copy has run.
     _copy_batch(device, srcs, dsts, sizes)
-    views = out.split(pieces)
-    return {i: _remember(views[2 * j], *fields) for j, (i, _, _, fields) in enumerate(items)}
+    views = _remember_views(out, [len(h) + nb for (_, _, h, _), nb in zip(items, nbs)], offs,
+                            [fields for _, _, _, fields in items])
+    return {i: v for (i, _, _, _), v in zip(items, views)}
 
 
 def compress_tensors(
@@ -738,7 +758,7 @@ def compress_tensors(
             stream.wait_stream(up)
             for x in xs:
                 x.record_stream(stream)
-        out, offs, sizes, temp = _launch_compress_batch(
+        out, offs, sizes, temp, fields = _launch_compress_batch(
             device, xs, [tensors[i] for i in idx], k, reorder, chunk_bytes, sub_chunks, passthrough_threshold)
         sizes_host = None
         if readback_to_cpu:  # each batch's sizes come back on their own, batches keep running
@@ -749,12 +769,14 @@ def compress_tensors(
         # The staged inputs and the scratch are only used on `stream` from here on, so the
         # caching allocator may hand their memory to later batches in stream order.
         del xs, temp
-        pending.append([idx, out, offs, sizes, sizes_host, done])
+        # Without readback, each blob will be a view into the batch buffer: made now, at its
+        # capacity, while the kernels run, and trimmed to the blob's size after the sync.
+        views = None if readback_to_cpu else out.split([b - a for a, b in zip(offs, offs[1:] + [out.numel()])])
+        pending.append([idx, out, offs, sizes, sizes_host, done, fields, views])
 
     # Coded tensors are launched in batches of one element size as the list is read (the first
     # batch smaller), so that the GPU starts while the host reads the rest.
     cur: dict[tuple[int, bool], tuple[list[int], int]] = {}
-    total = sum(t.numel() * t.element_size() for t in tensors)
     with contextlib.ExitStack() as ctx:
         for i, t in enumerate(tensors):
             if i == 0:  # the scalar arguments once, then each tensor's dtype and rank
@@ -775,7 +797,7 @@ def compress_tensors(
             key = (k, t.dtype in _REORDER)
             idx, nbytes = cur.get(key, ([], 0))
             limit = _DEVICE_BATCH_BYTES if t.is_cuda else _PIPELINE_BYTES
-            if idx and nbytes + n * k > _batch_limit(limit, len(pending), total):
+            if idx and nbytes + n * k > _batch_limit(limit, len(pending)):
                 launch(key[0], key[1], idx)
                 idx, nbytes = [], 0
             idx.append(i)
@@ -796,23 +818,22 @@ def compress_tensors(
         if not readback_to_cpu:
             all_sizes = torch.cat([p[3] for p in pending]).cpu().tolist()  # the one synchronization
             pos = 0
-            for idx, out, offs, *_ in pending:
-                # One split of the batch buffer into (blob, gap) pieces makes every view at once.
-                pieces = []
-                for j, o in enumerate(offs):
-                    size = all_sizes[pos + j]
-                    nxt = offs[j + 1] if j + 1 < len(offs) else out.numel()
-                    pieces += (size, nxt - o - size)
-                views = out.split(pieces)
+            for idx, out, offs, _, _, _, fields, views in pending:
+                n_b = len(idx)
+                for j in range(n_b):
+                    views[j].resize_(all_sizes[pos + j])  # shrinks the view; the storage stays
+                # The views share the buffer's version counter (bumped by each resize_), and each
+                # view's address and size follow from the offsets: records as _remember makes them.
+                ver, base = out._version, out.data_ptr()
                 for j, i in enumerate(idx):
-                    t = tensors[i]
-                    blobs[i] = _remember(views[2 * j], t.dtype, tuple(t.shape),
-                                         _FLAG_REORDER if t.dtype in _REORDER else 0, chunk_bytes, t.numel())
-                pos += len(idx)
+                    v = views[j]
+                    v._zn_header = (ver, base + offs[j], all_sizes[pos + j]) + fields[j]
+                    blobs[i] = v
+                pos += n_b
             return blobs  # type: ignore[return-value]
         copy_out = _side_stream(device, 1)
         for entry in pending:
-            idx, out, offs, _, sizes_host, done = entry
+            idx, out, offs, _, sizes_host, done, _, _ = entry
             done.synchronize()
             sizes_b = sizes_host.tolist()
             if pin_memory:  # one pinned buffer per batch (cheaper than one pinned allocation per blob)
@@ -841,15 +862,18 @@ def compress_tensors(
 def _launch_compress_batch(device, xs, srcs, k, reorder, chunk_bytes, sub_chunks, threshold):
     """zn_compress_batch for device tensors `xs` (flat, 16-byte aligned; `srcs` the original
     tensors, for the headers) on the current stream: one blob buffer holding every blob at
-    offs[j] (capacity zn_compress_bound each) and a device int64 size per blob."""
+    offs[j] (capacity zn_compress_bound each), a device int64 size per blob, the scratch, and the
+    header fields of each blob (for _remember_views)."""
     flags = _FLAG_REORDER if reorder else 0
-    heads, caps, offs, ns = [], [], [], []
+    heads, caps, offs, ns, fields = [], [], [], [], []
     total_cap = 0
     for x, t in zip(xs, srcs):
-        heads.append(_header(t, flags, chunk_bytes, 0))
+        shape = tuple(t.shape)
+        heads.append(_header_bytes(t.dtype, shape, flags, chunk_bytes, 0))
         n = x.numel()
         ns.append(n)
-        cap = int(_lib.lib.zn_compress_bound(n, k, t.dim(), chunk_bytes))
+        fields.append((t.dtype, shape, flags, chunk_bytes, n))
+        cap = int(_lib.lib.zn_compress_bound(n, k, len(shape), chunk_bytes))
         caps.append(cap)
         offs.append(total_cap)
         total_cap += (cap + 255) & ~255
@@ -875,7 +899,7 @@ def _launch_compress_batch(device, xs, srcs, k, reorder, chunk_bytes, sub_chunks
         ),
         "zn_compress_batch",
     )
-    return out, offs, sizes, temp
+    return out, offs, sizes, temp, fields
 
 
 def decompress_tensors(
@@ -893,34 +917,47 @@ def decompress_tensors(
 
     `out`, if given, has one entry per blob: None (allocate, as above) or the caller's tensor to
     decode into, with decompress_tensor's rules for `out` (on the call's compute device without
-    readback_to_cpu); the returned list then holds those tensors."""
+    readback_to_cpu); the returned list then holds those tensors.  Blobs are checked as the list is
+    read, so an invalid blob raises after the batches before it may have been launched (their
+    results are dropped)."""
     compute_device = _check_device(compute_device)
     if out is not None and len(out) != len(blobs):
         raise ValueError("out must have one entry per blob")
     dest = list(out) if out is not None else [None] * len(blobs)
     outs: list[torch.Tensor | None] = [None] * len(blobs)
-    # Headers of GPU blobs come to the host in one copy per device; prefixes[i] = (buffer, offset).
-    # Unchanged GPU blobs made by this module carry their header fields (_remember); only the others
-    # are read back.
-    plen = [0] * len(blobs)
-    prefixes: list[tuple[memoryview, int] | None] = [None] * len(blobs)
-    known = [None] * len(blobs)
-    by_dev: dict[torch.device, list[int]] = {}
-    for i, blob in enumerate(blobs):
-        if blob.dtype != torch.uint8 or blob.dim() != 1:
-            raise ValueError("blob must be a 1-D uint8 tensor")
-        plen[i] = p = min(blob.numel(), _FIXED.size + 8 * _MAX_NDIM)
-        known[i] = _known_header(blob)
-        if known[i] is not None:
-            continue
-        if blob.is_cuda:
-            by_dev.setdefault(blob.device, []).append(i)
-        else:
-            prefixes[i] = (memoryview(blob[:p].contiguous().numpy()), 0)
-    for dev, idx in by_dev.items():
-        flat, offs = _gather_prefixes(dev, [blobs[i] for i in idx], [plen[i] for i in idx])
-        for i, o in zip(idx, offs):
-            prefixes[i] = (flat, o)
+    # Header fields, read as the list is walked: unchanged GPU blobs made by this module carry
+    # theirs (_remember); the other GPU blobs' headers come to the host in one copy per device when
+    # the first of them is reached (prefixes[i] = (buffer, offset, length)); CPU blobs are read in
+    # place.
+    prefixes: list[tuple[memoryview, int, int] | None] = [None] * len(blobs)
+    plen_max = _FIXED.size + 8 * _MAX_NDIM
+
+    def fetch_prefixes(i: int) -> None:
+        """The prefixes of blob i and of every later GPU blob on its device without a record."""
+        dev = blobs[i].device
+        idx = [j for j in range(i, len(blobs))
+               if prefixes[j] is None and blobs[j].is_cuda and blobs[j].device == dev
+               and blobs[j].dtype == torch.uint8 and blobs[j].dim() == 1
+               and (j == i or _known_header(blobs[j]) is None)]
+        plens = [min(blobs[j].numel(), plen_max) for j in idx]
+        flat, offs = _gather_prefixes(dev, [blobs[j] for j in idx], plens)
+        for j, o, p in zip(idx, offs, plens):
+            prefixes[j] = (flat, o, p)
+
+    def header(i: int, blob: torch.Tensor) -> tuple:
+        """(dtype, shape, flags, chunk_bytes, n_comp, n) of blob i; n_comp = -1: the device reads it."""
+        h = _known_header(blob)
+        if h is not None:
+            dtype, shape, flags, chunk_bytes, n = h
+            return dtype, shape, flags, chunk_bytes, -1, n
+        if prefixes[i] is None:
+            if blob.is_cuda:
+                fetch_prefixes(i)
+            else:
+                p = min(blob.numel(), plen_max)
+                prefixes[i] = (memoryview(blob[:p].contiguous().numpy()), 0, p)
+        return _parse_header(*prefixes[i])
+
     small: list[tuple[int, torch.dtype, tuple[int, ...], int]] = []  # stored / empty, after the launches
 
     def decompress_small() -> None:
@@ -982,7 +1019,6 @@ def decompress_tensors(
     pos = 0
     launched = 0  # sub-batches launched so far
     cur: dict[tuple[int, bool], tuple[list, int]] = {}
-    total = sum(b.numel() for b in blobs)
 
     def launch(k: int, reorder: bool, items: list) -> None:
         nonlocal copy_in, pos, launched
@@ -1005,7 +1041,7 @@ def decompress_tensors(
                     if x.data_ptr() % 8:
                         x = x.clone()
                 xs.append(x)
-            if any(blobs[i].is_pinned() for i, _ in items):
+            if host and any(blobs[i].is_pinned() for i, _ in items):
                 ev = torch.cuda.Event()
                 ev.record(up)
                 uploaded.append(ev)
@@ -1039,11 +1075,9 @@ def decompress_tensors(
             outs[i] = y
 
     for i, blob in enumerate(blobs):
-        if known[i] is not None:
-            dtype, shape, flags, chunk_bytes, n = known[i]
-            n_comp = -1  # read from the blob by the device
-        else:
-            dtype, shape, flags, chunk_bytes, n_comp, n = _parse_header(prefixes[i][0], prefixes[i][1], plen[i])
+        if blob.dtype != torch.uint8 or blob.dim() != 1:
+            raise ValueError("blob must be a 1-D uint8 tensor")
+        dtype, shape, flags, chunk_bytes, n_comp, n = header(i, blob)
         if dest[i] is not None:
             _check_out(dest[i], dtype, shape, readback_to_cpu)
             if dest[i].is_cuda and dest[i].device != _gpu(blob, compute_device):
@@ -1062,14 +1096,15 @@ def decompress_tensors(
         if device is None:
             device = _gpu(blob, compute_device)
             stream = torch.cuda.current_stream(device)
-            # One status word per coded blob of this call (last_decode_status ORs them).
-            status = torch.zeros(len(blobs), dtype=torch.int32, device=device)
+            # One status word per coded blob of this call, each set by the decoder (last_decode_status
+            # ORs the words of the coded blobs).
+            status = torch.empty(len(blobs), dtype=torch.int32, device=device)
         key = (k, bool(flags & _FLAG_REORDER))
         items, nbytes = cur.get(key, ([], 0))
         items.append((i, (dtype, shape, chunk_bytes, n_comp, n)))
         nbytes += blob.numel()
         limit = _PIPELINE_BYTES if not blob.is_cuda else _DEVICE_BATCH_BYTES
-        if nbytes >= _batch_limit(limit, launched, total):
+        if nbytes >= _batch_limit(limit, launched):
             with torch.cuda.device(device):
                 launch(key[0], key[1], items)
             items, nbytes = [], 0
@@ -1081,7 +1116,7 @@ def decompress_tensors(
         for (k, reorder), (items, _) in cur.items():
             if items:
                 launch(k, reorder, items)
-        _set_status(device, status)
+        _set_status(device, status[:pos])
         decompress_small()
         for ev in uploaded:
             ev.synchronize()

@@ -112,9 +112,9 @@ int zn_timing_enable(const char* kernel, int enable) {
 
 int zn_timing_read(const char* kernel, double* total_ms, int64_t* launches) {
   std::lock_guard<std::mutex> lock(zn::g_timing.mu);
-  // Launches of one kind may overlap (the Python layer runs a call's sub-batches on two streams),
-  // so the time is the union of their [start, stop] intervals, measured from the kind's first
-  // start event: the time during which at least one of them ran.
+  // Launches of one kind may overlap (callers that launch on several streams or threads), so the
+  // time is the union of their [start, stop] intervals, measured from the kind's first start
+  // event: the time during which at least one of them ran.
   std::vector<std::pair<double, double>> iv;
   std::vector<zn::Timing::Rec> keep;
   cudaEvent_t origin = nullptr;

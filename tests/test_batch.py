@@ -131,8 +131,7 @@ def test_many_sub_batches_keep_stream_order(monkeypatch):
     read on it just after (no synchronization in between) round-trip exactly."""
     from cuzipnn_b200 import _codec
 
-    monkeypatch.setattr(_codec, "_FIRST_BATCH_MIN", 1 << 16)
-    monkeypatch.setattr(_codec, "_FIRST_BATCH_MAX", 1 << 16)
+    monkeypatch.setattr(_codec, "_FIRST_BATCH", 1 << 16)
     monkeypatch.setattr(_codec, "_DEVICE_BATCH_BYTES", 1 << 20)
     g = torch.Generator(device="cuda").manual_seed(8)
     s = torch.cuda.Stream()
