@@ -601,10 +601,10 @@ _PIPELINE_BYTES = 1 << 29  # sub-batch of host-resident inputs (upload overlappe
 _DEVICE_BATCH_BYTES = 1 << 32  # sub-batch of device-resident inputs (launched while the host prepares the next)
 # The first sub-batch of a call is launched once _FIRST_BATCH bytes are read, so that the GPU
 # starts soon; each later one is _BATCH_GROWTH times larger (up to the batch limit), so that the
-# kernels of one batch run while the host prepares the next.  256 MB keep the kernels of the first
-# batch busy (~0.2 ms) for as long as the host needs to read and launch the next few hundred
-# tensors, without a pass over the whole list before the first launch.
-_FIRST_BATCH = 1 << 28
+# kernels of one batch run while the host prepares the next.  512 MB keep the kernels of the first
+# batch busy (0.3-0.5 ms) for as long as the host needs to read and launch the next hundred or so
+# tensors (a few microseconds each), and take the host only a few tensors of a model to gather.
+_FIRST_BATCH = 1 << 29
 _BATCH_GROWTH = 16
 
 
@@ -796,12 +796,12 @@ def compress_tensors(
                 stream = torch.cuda.current_stream(device)
             key = (k, t.dtype in _REORDER)
             idx, nbytes = cur.get(key, ([], 0))
-            limit = _DEVICE_BATCH_BYTES if t.is_cuda else _PIPELINE_BYTES
-            if idx and nbytes + n * k > _batch_limit(limit, len(pending)):
+            idx.append(i)
+            nbytes += n * k
+            if nbytes >= _batch_limit(_DEVICE_BATCH_BYTES if t.is_cuda else _PIPELINE_BYTES, len(pending)):
                 launch(key[0], key[1], idx)
                 idx, nbytes = [], 0
-            idx.append(i)
-            cur[key] = (idx, nbytes + n * k)
+            cur[key] = (idx, nbytes)
         if device is None:
             if small and not readback_to_cpu:
                 dev = _gpu(tensors[small[0]].detach(), cd)

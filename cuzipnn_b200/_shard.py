@@ -203,8 +203,9 @@ def compress_model_shard(
     whole_idx, split = plan if plan is not None else plan_model([_nbytes(t) for t in tensors], world, split_bytes)
     chunk = kwargs.get("chunk_bytes", C.DEFAULT_CHUNK_BYTES)
     minb = kwargs.get("min_compress_bytes", C.DEFAULT_MIN_COMPRESS_BYTES)
-    items, keys, parts = [tensors[i] for i in whole_idx[rank]], list(whole_idx[rank]), {}
-    part_keys = []
+    # The parts go first: they are large, so the call's first sub-batch fills (and its kernels
+    # start) after a tensor or two.
+    items, parts, part_keys = [], {}, []
     for i in split:
         t = tensors[i]
         if _nbytes(t) < minb or t.numel() == 0:  # the stored or the empty path: rank 0 holds it whole
@@ -217,9 +218,11 @@ def compress_model_shard(
             part_keys.append(i)
         else:  # a short (or empty) range is coded with min_compress_bytes = 0, as compress_chunk_range does
             parts[i] = compress_chunk_range(t, rank, world, **kwargs)
+    keys = list(whole_idx[rank])
+    items += [tensors[i] for i in keys]
     blobs = compress_tensors(items, **kwargs) if items else []
-    whole = dict(zip(keys, blobs[: len(keys)]))
-    parts.update(zip(part_keys, blobs[len(keys) :]))
+    parts.update(zip(part_keys, blobs[: len(part_keys)]))
+    whole = dict(zip(keys, blobs[len(part_keys) :]))
     return whole, parts
 
 
@@ -228,8 +231,8 @@ def decompress_model_shard(whole: dict[int, torch.Tensor], parts: dict[int, torc
     """Decompress what compress_model_shard returned, in one decompress_tensors call: (tensors by
     index, this rank's flat elements of each split tensor by index)."""
     wk, pk = sorted(whole), sorted(parts)
-    outs = decompress_tensors([whole[i] for i in wk] + [parts[i] for i in pk], **kwargs) if wk or pk else []
-    return dict(zip(wk, outs[: len(wk)])), {i: o.reshape(-1) for i, o in zip(pk, outs[len(wk) :])}
+    outs = decompress_tensors([parts[i] for i in pk] + [whole[i] for i in wk], **kwargs) if wk or pk else []
+    return dict(zip(wk, outs[len(pk) :])), {i: o.reshape(-1) for i, o in zip(pk, outs[: len(pk)])}
 
 
 class _Tables:
