@@ -91,9 +91,11 @@ def nbytes(ts) -> int:
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock, power and throttle reasons during the timed region."""
+    """nvidia-smi samples of SM clock, power and throttle reasons.  The sampler starts before the
+    warm-up (nvidia-smi takes a while to start, longer with eight of them at once), and only the
+    samples stamped inside the timed region (window()) are summarised."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -101,6 +103,7 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
@@ -114,6 +117,10 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def window(self, t0: float, t1: float) -> None:
+        """The timed region, as time.time() values."""
+        self.t0, self.t1 = t0, t1
+
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
@@ -124,12 +131,20 @@ class ClockSampler:
         return False
 
     def summary(self) -> dict:
+        import datetime
+
         rows = []
         try:
             for line in open(self.path):
                 f = [v.strip() for v in line.split(",")]
-                if len(f) >= 9 and f[1].replace(".", "").isdigit():
-                    rows.append(f)
+                if len(f) < 10 or not f[2].replace(".", "").isdigit():
+                    continue
+                try:
+                    ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    continue
+                if self.t0 is None or self.t0 <= ts <= self.t1:
+                    rows.append(f[1:])
             os.unlink(self.path)
         except OSError:
             pass
@@ -362,13 +377,15 @@ def main() -> None:
     ratio = blob_bytes / model_bytes
     del blobs, outs
 
+    clocks = ClockSampler(local).__enter__()  # running through the warm-up, summarised over the timed region
     for _ in range(args.warmup):
         step()
     barrier()
     launches0 = _lib.launch_count()
     ev = []
-    with ClockSampler(local) as clocks, _lib.KernelTimer() as kt:
+    with _lib.KernelTimer() as kt:
         barrier()
+        w0 = time.time()
         for _ in range(args.steps):
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
@@ -378,6 +395,8 @@ def main() -> None:
             ev.append((a, mid, b))
             del blobs, outs
         barrier()
+        clocks.window(w0, time.time())
+    clocks.__exit__(None, None, None)
     gpu_launches = _lib.launch_count() - launches0
     t_step = sum(a.elapsed_time(b) for a, _, b in ev) / len(ev) / 1e3
     t_comp = sum(a.elapsed_time(m) for a, m, _ in ev) / len(ev) / 1e3
