@@ -144,24 +144,22 @@ def _remember(blob: torch.Tensor, dtype: torch.dtype, shape: tuple[int, ...], fl
     return blob
 
 
-def _remember_views(out: torch.Tensor, sizes: list[int], offs: list[int], fields: list[tuple]) -> list[torch.Tensor]:
-    """Blobs of one batch buffer: the view out[offs[j] : offs[j] + sizes[j]] of each, made by one
-    split, each remembering fields[j] = (dtype, shape, flags, chunk_bytes, n) as _remember does.
-    Views share the buffer's version counter, and each view's address and size follow from the
-    offsets, so no view is asked for them."""
-    pieces = []
-    end = out.numel()
-    for j, o in enumerate(offs):
-        nxt = offs[j + 1] if j + 1 < len(offs) else end
-        pieces += (sizes[j], nxt - o - sizes[j])
-    views = out.split(pieces)
+def _capacity_views(out: torch.Tensor, offs: list[int]) -> tuple[torch.Tensor, ...]:
+    """One view of `out` per region [offs[j], offs[j + 1]) (the last to the end), by one split."""
+    return out.split([b - a for a, b in zip(offs, offs[1:] + [out.numel()])])
+
+
+def _trim_and_remember(out: torch.Tensor, views, sizes: list[int], offs: list[int], fields: list[tuple]) -> None:
+    """Trim each capacity view of `out` to its blob's size (resize_ shrinks a view in place; the
+    storage stays) and give it the record _remember makes, fields[j] = (dtype, shape, flags,
+    chunk_bytes, n).  The views share the buffer's version counter (bumped by each resize_, so it
+    is read after them), and each view's address and size follow from the offsets, so no view is
+    asked for them."""
+    for v, size in zip(views, sizes):
+        v.resize_(size)
     ver, base = out._version, out.data_ptr()
-    blobs = []
-    for j, f in enumerate(fields):
-        v = views[2 * j]
-        v._zn_header = (ver, base + offs[j], sizes[j]) + f
-        blobs.append(v)
-    return blobs
+    for v, o, size, f in zip(views, offs, sizes, fields):
+        v._zn_header = (ver, base + o, size) + f
 
 
 def _known_header(blob: torch.Tensor):
@@ -644,23 +642,23 @@ def _copy_batch(device: torch.device, srcs: list[int], dsts: list[int], sizes: l
     )
 
 
-def _stored_blobs_gpu(items: list[tuple[int, torch.Tensor, bytes, tuple]], device: torch.device) -> dict[int, torch.Tensor]:
+def _stored_blobs_gpu(items: list[tuple[int, torch.Tensor, int, bytes, tuple]], device: torch.device
+                      ) -> dict[int, torch.Tensor]:
     """Blobs of the stored path (header + raw bytes) for many tensors, built on the GPU by one
-    header upload and one batched copy.  items: (index, tensor, header, header fields for
-    _remember).  Each blob is a view into one shared buffer (256-byte aligned), all made by one
-    split of it."""
+    header upload and one batched copy.  items: (index, tensor, its bytes, header, header fields
+    for _remember).  Each blob is a view into one shared buffer (256-byte aligned)."""
     dev = device.index
-    nbs = [x.numel() * x.element_size() for _, x, _, _ in items]
     offs, pos = [], 0
-    for (_, _, head, _), nb in zip(items, nbs):
+    for _, _, nb, head, _ in items:
         offs.append(pos)
         pos += (len(head) + nb + 255) & ~255
     out = torch.empty(pos, dtype=torch.uint8, device=device)
-    hdev = torch.frombuffer(bytearray(b"".join(h for _, _, h, _ in items)), dtype=torch.uint8).pin_memory()
+    views = _capacity_views(out, offs)
+    hdev = torch.frombuffer(bytearray(b"".join(h for _, _, _, h, _ in items)), dtype=torch.uint8).pin_memory()
     hdev = hdev.to(device, non_blocking=True)
     srcs, dsts, sizes = [], [], []
     hpos, hbase, obase = 0, hdev.data_ptr(), out.data_ptr()
-    for (_, x, head, _), o, nb in zip(items, offs, nbs):
+    for (_, x, nb, head, _), o in zip(items, offs):
         hl = len(head)
         srcs.append(hbase + hpos)
         dsts.append(obase + o)
@@ -668,7 +666,7 @@ def _stored_blobs_gpu(items: list[tuple[int, torch.Tensor, bytes, tuple]], devic
         hpos += hl
         if nb:
             if not (x.is_cuda and x.get_device() == dev and x.is_contiguous() and x.data_ptr() % 8 == 0):
-                x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
+                x = x.detach().to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
                 if x.data_ptr() % 8:
                     x = x.clone()
             srcs.append(x.data_ptr())
@@ -677,9 +675,8 @@ def _stored_blobs_gpu(items: list[tuple[int, torch.Tensor, bytes, tuple]], devic
     # `hdev` and the staged inputs were allocated on this stream, so the caching allocator reuses
     # their memory only after the copy has run.
     _copy_batch(device, srcs, dsts, sizes)
-    views = _remember_views(out, [len(h) + nb for (_, _, h, _), nb in zip(items, nbs)], offs,
-                            [fields for _, _, _, fields in items])
-    return {i: v for (i, _, _, _), v in zip(items, views)}
+    _trim_and_remember(out, views, [len(h) + nb for _, _, nb, h, _ in items], offs, [f for *_, f in items])
+    return {it[0]: v for it, v in zip(items, views)}
 
 
 def compress_tensors(
@@ -704,21 +701,21 @@ def compress_tensors(
     is read, so an invalid tensor raises after the batches before it may have been launched (their
     results are dropped)."""
     blobs: list[torch.Tensor | None] = [None] * len(tensors)
-    small: list[int] = []  # stored path and empty tensors, handled after the coded launches
+    small: list[tuple[int, int, int]] = []  # (index, element size, numel) of the stored path and empty tensors, handled after the coded launches
     sub_chunks = _sub_chunks(chunk_bytes, sub_chunk_bytes) if sub_chunk_bytes > 0 else 0
     cd = _check_device(compute_device)
 
     def compress_small(device: torch.device | None) -> None:
         batch = []
-        for i in small:
+        for i, k, n in small:
             t = tensors[i]
-            k, n = t.element_size(), t.numel()
             if (device is not None and not readback_to_cpu and n * k <= _COPY_BATCH_MAX
                     and (t.get_device() == device.index if cd is None and t.is_cuda else _gpu(t, cd) == device)):
                 stored = n * k < min_compress_bytes
-                flags = _FLAG_STORED if stored else _FLAG_REORDER if t.dtype in _REORDER else 0
+                dtype, shape = t.dtype, tuple(t.shape)
+                flags = _FLAG_STORED if stored else _FLAG_REORDER if dtype in _REORDER else 0
                 cbf = 0 if stored else chunk_bytes
-                batch.append((i, t.detach(), _header(t, flags, cbf, 0), (t.dtype, tuple(t.shape), flags, cbf, n)))
+                batch.append((i, t, n * k, _header_bytes(dtype, shape, flags, cbf, 0), (dtype, shape, flags, cbf, n)))
             else:
                 blobs[i] = compress_tensor(t, chunk_bytes=chunk_bytes, sub_chunk_bytes=sub_chunk_bytes,
                                            passthrough_threshold=passthrough_threshold,
@@ -771,7 +768,7 @@ def compress_tensors(
         del xs, temp
         # Without readback, each blob will be a view into the batch buffer: made now, at its
         # capacity, while the kernels run, and trimmed to the blob's size after the sync.
-        views = None if readback_to_cpu else out.split([b - a for a, b in zip(offs, offs[1:] + [out.numel()])])
+        views = None if readback_to_cpu else _capacity_views(out, offs)
         pending.append([idx, out, offs, sizes, sizes_host, done, fields, views])
 
     # Coded tensors are launched in batches of one element size as the list is read (the first
@@ -788,7 +785,7 @@ def compress_tensors(
                 raise ValueError(f"at most {_MAX_NDIM} dimensions are supported")
             k, n = t.element_size(), t.numel()
             if n * k < min_compress_bytes or n == 0:
-                small.append(i)
+                small.append((i, k, n))
                 continue
             if device is None:
                 device = _gpu(t.detach(), cd)
@@ -804,7 +801,7 @@ def compress_tensors(
             cur[key] = (idx, nbytes)
         if device is None:
             if small and not readback_to_cpu:
-                dev = _gpu(tensors[small[0]].detach(), cd)
+                dev = _gpu(tensors[small[0][0]].detach(), cd)
                 with torch.cuda.device(dev):
                     compress_small(dev)
             else:
@@ -819,17 +816,10 @@ def compress_tensors(
             all_sizes = torch.cat([p[3] for p in pending]).cpu().tolist()  # the one synchronization
             pos = 0
             for idx, out, offs, _, _, _, fields, views in pending:
-                n_b = len(idx)
-                for j in range(n_b):
-                    views[j].resize_(all_sizes[pos + j])  # shrinks the view; the storage stays
-                # The views share the buffer's version counter (bumped by each resize_), and each
-                # view's address and size follow from the offsets: records as _remember makes them.
-                ver, base = out._version, out.data_ptr()
-                for j, i in enumerate(idx):
-                    v = views[j]
-                    v._zn_header = (ver, base + offs[j], all_sizes[pos + j]) + fields[j]
+                _trim_and_remember(out, views, all_sizes[pos : pos + len(idx)], offs, fields)
+                for i, v in zip(idx, views):
                     blobs[i] = v
-                pos += n_b
+                pos += len(idx)
             return blobs  # type: ignore[return-value]
         copy_out = _side_stream(device, 1)
         for entry in pending:
@@ -863,7 +853,7 @@ def _launch_compress_batch(device, xs, srcs, k, reorder, chunk_bytes, sub_chunks
     """zn_compress_batch for device tensors `xs` (flat, 16-byte aligned; `srcs` the original
     tensors, for the headers) on the current stream: one blob buffer holding every blob at
     offs[j] (capacity zn_compress_bound each), a device int64 size per blob, the scratch, and the
-    header fields of each blob (for _remember_views)."""
+    header fields of each blob (for _trim_and_remember)."""
     flags = _FLAG_REORDER if reorder else 0
     heads, caps, offs, ns, fields = [], [], [], [], []
     total_cap = 0
@@ -963,7 +953,8 @@ def decompress_tensors(
     def decompress_small() -> None:
         """Stored blobs on the GPU decode into GPU tensors by one batched copy; the rest (CPU blobs,
         CPU outputs, empty tensors) take decompress_tensor."""
-        srcs, dsts, sizes, tiny = [], [], [], []
+        srcs, dsts, sizes = [], [], []
+        tiny: dict[torch.dtype, list] = {}  # outputs placed in one buffer per dtype below
         bdev = None  # the one device (index) whose stored blobs are batched
         if compute_device is None:
             cdi = None
@@ -975,16 +966,17 @@ def decompress_tensors(
             nbytes = math.prod(shape) * dtype.itemsize
             bi = b.get_device() if b.is_cuda else None
             d = dest[i]
+            src = b.data_ptr() + header_size
             if (flags & _FLAG_STORED and bi is not None and not readback_to_cpu and 0 < nbytes <= _COPY_BATCH_MAX
-                    and (b.data_ptr() + header_size) % 8 == 0 and cdi in (None, bi) and bdev in (None, bi)
+                    and src % 8 == 0 and cdi in (None, bi) and bdev in (None, bi)
                     and (d is None or (d.is_cuda and d.get_device() == bi and d.data_ptr() % 8 == 0))):
                 bdev = bi
                 if b.numel() < header_size + nbytes:
                     raise ValueError("blob is truncated")
-                srcs.append(b.data_ptr() + header_size)
+                srcs.append(src)
                 sizes.append(nbytes)
-                if d is None and nbytes <= _TINY_BYTES:  # placed in one shared buffer below
-                    tiny.append((i, dtype, shape, nbytes, len(dsts)))
+                if d is None and nbytes <= _TINY_BYTES:
+                    tiny.setdefault(dtype, []).append((i, shape, nbytes // dtype.itemsize, len(dsts)))
                     dsts.append(0)
                 else:
                     y = torch.empty(shape, dtype=dtype, device=b.device) if d is None else d
@@ -995,18 +987,20 @@ def decompress_tensors(
                                             out=d)
         if srcs:
             dev = torch.device("cuda", bdev)
-            if tiny:
-                pieces, pos = [], 0
-                for _, _, _, nb, j in tiny:
-                    step = (nb + 255) & ~255
-                    pieces += (nb, step - nb)
-                    pos += step
-                buf = torch.empty(pos, dtype=torch.uint8, device=dev)
-                views, base, pos = buf.split(pieces), buf.data_ptr(), 0
-                for q, (i, dtype, shape, nb, j) in enumerate(tiny):
-                    outs[i] = views[2 * q].view(dtype).view(shape)
-                    dsts[j] = base + pos
-                    pos += (nb + 255) & ~255
+            for dtype, group in tiny.items():
+                # Each output is a view of its region (256-byte aligned) of one buffer, shaped in
+                # place by resize_ (the storage stays): one tensor made per output.
+                step = 256 // dtype.itemsize
+                offs, pos = [], 0
+                for _, _, numel, _ in group:
+                    offs.append(pos)
+                    pos += -(-numel // step) * step
+                buf = torch.empty(pos, dtype=dtype, device=dev)
+                base, isz = buf.data_ptr(), dtype.itemsize
+                for v, o, (i, shape, _, j) in zip(_capacity_views(buf, offs), offs, group):
+                    v.resize_(shape)
+                    outs[i] = v
+                    dsts[j] = base + o * isz
             with torch.cuda.device(dev):
                 _copy_batch(dev, srcs, dsts, sizes)
 
