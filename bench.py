@@ -287,7 +287,8 @@ def run_reference(args) -> None:
         "data": "synthetic",
         "config": {"workload": WORKLOAD, "sample": "layer 0 (466 MB) per step", "ratio": round(nout / nin, 5)},
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": "compress + decompress of layer 0 (466 MB) with the C oracle (OpenMP)"},
+                         "sample": "compress + decompress of layer 0 (466 MB) with the C oracle (OpenMP)",
+                         "note": "the C oracle: the scalar correctness checker of the tests, run on all host threads; not a tuned CPU codec, so ratios against it say nothing about the kernels"},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -422,6 +423,7 @@ def main() -> None:
     traffic = round(tr * algo) if tr else None
     roofline = {"bound": "hbm", "kernel": dominant + "_kernel", "achieved": round(achieved, 1),
                 "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "frac_of_8tbs_nominal": round(achieved / 8000.0, 4),
                 "traffic": traffic, "algo_bytes_per_step": algo, "traffic_basis": "per step (all launches)",
                 "kernel_ms_per_step": round(step_s * 1e3, 4), "launches_per_step": round(dom_n / args.steps, 2),
                 "kernel_share": {k: round(v[0] / sum(x[0] for x in times.values()), 4) for k, v in times.items()}}
@@ -532,7 +534,8 @@ def main() -> None:
         threads = os.cpu_count() or 1
         tc, td, nin, _ = cpu_round_trip(cpu_sample(), threads)
         cpu_baseline = {"value": round(nin / (tc + td) / GB, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                        "sample": "compress + decompress of layer 0 (466 MB) with the C oracle (OpenMP)"}
+                        "sample": "compress + decompress of layer 0 (466 MB) with the C oracle (OpenMP)",
+                        "note": "the C oracle: the scalar correctness checker of the tests, run on all host threads; not a tuned CPU codec, so ratios against it say nothing about the kernels"}
 
     barrier()
     if rank == 0:
