@@ -171,3 +171,66 @@ def test_large_pageable_host_copies():
     assert torch.equal(outs[2], x[:1000])
     h = z.hash_tensor_with_crc32(x, checksum_chunk_bytes=1 << 20)
     assert torch.equal(h, z.hash_tensor_with_crc32(x.cuda(), checksum_chunk_bytes=1 << 20))
+
+
+def test_blob_records_and_headers_read_as_the_list_is_walked():
+    """GPU blobs made by the batched call carry their header records (size, address and fields of
+    the trimmed view); a list mixing recorded blobs with GPU blobs that have none (clones, written
+    in place) and CPU blobs decodes exactly, whatever their order; an invalid blob after valid ones
+    raises."""
+    ts = mixed_tensors()
+    ref = z.compress_tensors(ts)  # CPU blobs
+    blobs = z.compress_tensors(ts, readback_to_cpu=False)
+    for t, b, r in zip(ts, blobs, ref):
+        assert b.is_cuda and b.is_contiguous() and b.numel() == r.numel()
+        assert torch.equal(b.cpu(), r)
+        h = b._zn_header
+        assert (h[0], h[1], h[2]) == (b._version, b.data_ptr(), b.numel())
+        assert h[3] == t.dtype and h[4] == tuple(t.shape)
+    mix = []
+    for j, (b, r) in enumerate(zip(blobs, ref)):
+        if j % 3 == 1:
+            mix.append(b.clone())  # no record: its header is gathered from the device
+        elif j % 3 == 2:
+            mix.append(r)          # a CPU blob
+        else:
+            mix.append(b)
+    bumped = blobs[0]
+    bumped[:1].copy_(bumped[:1])   # an in-place write voids its record (same bytes)
+    mix.append(bumped)
+    outs = z.decompress_tensors(mix)
+    torch.cuda.synchronize()
+    assert z.last_decode_status() == 0
+    for t, y in zip(ts + [ts[0]], outs):
+        assert y.shape == t.shape and y.dtype == t.dtype
+        assert torch.equal(bits(y.cpu()), bits(t.cpu()))
+    with pytest.raises(ValueError, match="1-D uint8"):
+        z.decompress_tensors([blobs[0], blobs[2], blobs[4].view(torch.int8)])
+
+
+def test_tiny_stored_outputs_of_many_dtypes_and_shapes():
+    """Stored-path tensors of every element size and of 0-d, 1-d and 3-d shapes, mixed with coded
+    ones, come back exact, contiguous and with their own shapes from one batched call (the tiny
+    ones are views of one buffer per dtype, shaped in place)."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    ts = []
+    for dtype in [torch.bool, torch.uint8, torch.int8, torch.float16, torch.bfloat16, torch.int32,
+                  torch.float32, torch.int64, torch.float64, torch.complex64, torch.float8_e5m2]:
+        for shape in [(), (1,), (7,), (3, 5, 2), (1000,), (4, 33, 3)]:
+            x = torch.randn(shape, device="cuda", generator=g) if dtype != torch.complex64 else torch.randn(
+                shape, device="cuda", generator=g, dtype=torch.complex64)
+            ts.append(x.to(dtype) if dtype != torch.bool else x > 0)
+    ts.insert(5, (torch.randn(300, 1000, device="cuda", generator=g) * 0.02).to(torch.bfloat16))  # coded
+    blobs = z.compress_tensors(ts, readback_to_cpu=False)
+    for t, b in zip(ts, blobs):
+        assert torch.equal(b.cpu(), z.compress_tensor(t))
+    outs = z.decompress_tensors(blobs)
+    torch.cuda.synchronize()
+    assert z.last_decode_status() == 0
+    for t, y in zip(ts, outs):
+        assert y.shape == t.shape and y.dtype == t.dtype and y.is_contiguous() and y.is_cuda
+        assert torch.equal(y.view(-1).view(torch.uint8), t.reshape(-1).view(torch.uint8))
+    # The outputs are independent: writing one leaves the others alone.
+    outs[0].fill_(True)  # a 0-d bool tensor
+    for t, y in zip(ts[1:], outs[1:]):
+        assert torch.equal(y.view(-1).view(torch.uint8), t.reshape(-1).view(torch.uint8))
