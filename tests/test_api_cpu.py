@@ -154,3 +154,27 @@ def test_stored_crc_on_host():
     x = w(1000)
     blob, crc = z.compress_tensor_with_crc32(x, checksum_chunk_bytes=100)
     assert crc.tolist() == O.crc32_segments(blob.numpy(), 100).tolist()
+
+
+def test_trimmed_views_carry_the_records_remember_makes():
+    """The batched calls' blob views (capacity views of one buffer, trimmed in place) hold exactly
+    their bytes and the same header records _remember computes from the views themselves; a later
+    in-place write to any view of the buffer voids every record."""
+    from cuzipnn_b200 import _codec as C
+
+    out = torch.arange(5000, dtype=torch.int64).to(torch.uint8)
+    offs, sizes = [0, 1024, 2048, 4096], [1000, 17, 2048, 904]
+    fields = [(torch.bfloat16, (3, 4), 1, 131072, 12), (torch.float32, (5,), 0, 131072, 5),
+              (torch.uint8, (2048,), 2, 0, 2048), (torch.float16, (), 0, 4096, 1)]
+    views = C._capacity_views(out, offs)
+    assert [v.numel() for v in views] == [1024, 1024, 2048, 904]
+    C._trim_and_remember(out, views, sizes, offs, fields)
+    for v, o, n, f in zip(views, offs, sizes, fields):
+        assert v.numel() == n and v.is_contiguous()
+        assert torch.equal(v, out[o : o + n])
+        rec = v._zn_header
+        C._remember(v, *f)
+        assert rec == v._zn_header
+        assert C._known_header(v) is None  # a CPU tensor: records only apply to GPU blobs
+    views[1].add_(0)  # in place: the shared version counter moves for every view
+    assert all(v._zn_header[0] != v._version for v in views)
