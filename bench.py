@@ -330,6 +330,9 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    if local_world > 1:  # each rank's host copies (pageable blobs) get its share of the host cores
+        torch.set_num_threads(max(1, (os.cpu_count() or 1) // local_world))
     dist = None
     if world > 1:
         import datetime
