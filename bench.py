@@ -431,6 +431,38 @@ def main() -> None:
                 "kernel_ms_per_step": round(step_s * 1e3, 4), "launches_per_step": round(dom_n / args.steps, 2),
                 "kernel_share": {k: round(v[0] / sum(x[0] for x in times.values()), 4) for k, v in times.items()}}
 
+    # Strong scaling: one copy of the model over the ranks (plan_model: tensors above half a rank's
+    # mean share split by chunk range, the rest whole, longest first): device time of
+    # compress_model_shard + decompress_model_shard, max over ranks, 3 warm-up + 5 timed passes.
+    # Measured before the sections with host copies, whose copy threads can keep the host busy
+    # afterwards while several ranks run.
+    strong = None
+    if not args.no_strong:
+        plan = z.plan_model([t.numel() * t.element_size() for t in model], world)  # once per model
+        tc_, td_ = [], []
+        for s_i in range(8):
+            barrier()
+            a = torch.cuda.Event(enable_timing=True)
+            m = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            whole, parts = z.compress_model_shard(model, rank, world, plan=plan, readback_to_cpu=False)
+            m.record()
+            outs, pouts = z.decompress_model_shard(whole, parts)
+            b.record()
+            torch.cuda.synchronize()
+            if s_i >= 3:
+                tc_.append(a.elapsed_time(m) / 1e3)
+                td_.append(m.elapsed_time(b) / 1e3)
+            del whole, parts, outs, pouts
+        sc, sd = max_over_ranks(sum(tc_) / len(tc_)), max_over_ranks(sum(td_) / len(td_))
+        st = max_over_ranks(sum(c + d for c, d in zip(tc_, td_)) / len(tc_))
+        strong = {"value": round(model_bytes / st / GB, 3), "unit": "GB/s", "ms_per_step": round(st * 1e3, 3),
+                  "compress_gbs": round(model_bytes / sc / GB, 3), "decompress_gbs": round(model_bytes / sd / GB, 3),
+                  "scaling": "strong", "split_tensors": len(plan[1]),
+                  "workload": "one copy of the model over the ranks (plan_model: tensors above half a rank's "
+                              "share split by chunk range, the rest whole, longest first)"}
+
     # One tensor at a time (the reference's own methodology), device time.
     ev1 = []
     for _ in range(0 if args.no_one_at_a_time else 1):
@@ -471,36 +503,6 @@ def main() -> None:
                   "decompress_gbs": round(world * model_bytes / rd_ / GB, 3),
                   "path": "GPU tensor -> compress_tensor() defaults (CPU blob) -> decompress_tensor(blob, compute_device) "
                           "one tensor at a time, best of 2 passes, wall clock"}
-
-    # Strong scaling: one copy of the model over the ranks (plan_model: tensors above half a rank's
-    # mean share split by chunk range, the rest whole, longest first): device time of
-    # compress_model_shard + decompress_model_shard, max over ranks, 3 warm-up + 5 timed passes.
-    strong = None
-    if not args.no_strong:
-        plan = z.plan_model([t.numel() * t.element_size() for t in model], world)  # once per model
-        tc_, td_ = [], []
-        for s_i in range(8):
-            barrier()
-            a = torch.cuda.Event(enable_timing=True)
-            m = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record()
-            whole, parts = z.compress_model_shard(model, rank, world, plan=plan, readback_to_cpu=False)
-            m.record()
-            outs, pouts = z.decompress_model_shard(whole, parts)
-            b.record()
-            torch.cuda.synchronize()
-            if s_i >= 3:
-                tc_.append(a.elapsed_time(m) / 1e3)
-                td_.append(m.elapsed_time(b) / 1e3)
-            del whole, parts, outs, pouts
-        sc, sd = max_over_ranks(sum(tc_) / len(tc_)), max_over_ranks(sum(td_) / len(td_))
-        st = max_over_ranks(sum(c + d for c, d in zip(tc_, td_)) / len(tc_))
-        strong = {"value": round(model_bytes / st / GB, 3), "unit": "GB/s", "ms_per_step": round(st * 1e3, 3),
-                  "compress_gbs": round(model_bytes / sc / GB, 3), "decompress_gbs": round(model_bytes / sd / GB, 3),
-                  "scaling": "strong", "split_tensors": len(plan[1]),
-                  "workload": "one copy of the model over the ranks (plan_model: tensors above half a rank's "
-                              "share split by chunk range, the rest whole, longest first)"}
 
     # End to end through the public API from pinned host memory: H2D of the inputs, CPU blobs,
     # H2D of the blobs, and a D2H read of a result word each step.
