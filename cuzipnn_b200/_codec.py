@@ -737,7 +737,7 @@ def compress_tensors(
         if host and copy_in is None:
             copy_in = _side_stream(device, 0)
         up = copy_in if host else stream
-        with torch.cuda.stream(up):
+        with torch.cuda.stream(up) if host else contextlib.nullcontext():  # `stream` is current already
             xs = []
             dev = device.index
             for i in idx:
@@ -1021,7 +1021,7 @@ def decompress_tensors(
         if host and copy_in is None:
             copy_in = _side_stream(device, 0)
         up = copy_in if host else stream
-        with torch.cuda.stream(up):
+        with torch.cuda.stream(up) if host else contextlib.nullcontext():  # `stream` is current already
             xs = []
             dev = device.index
             for i, _ in items:

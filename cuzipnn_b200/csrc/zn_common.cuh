@@ -222,29 +222,31 @@ __device__ __forceinline__ int find_job(const J* __restrict__ jobs, int njobs, i
   return __ldg(map + gchunk);
 }
 
-// Fill the chunk -> job map: CTA i writes i over job i's chunk range [chunk0_i, chunk0_{i+1}).
-template <class J>
-__global__ void map_jobs_kernel(const J* __restrict__ jobs, int njobs, int64_t total_chunks) {
-  int32_t* map = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(const_cast<J*>(jobs)) + job_structs_bytes<J>(njobs));
-  const int i = blockIdx.x;
-  const int64_t c0 = jobs[i].chunk0, c1 = i + 1 < njobs ? jobs[i + 1].chunk0 : total_chunks;
-  for (int64_t c = c0 + threadIdx.x; c < c1; c += blockDim.x) map[c] = i;
-}
-
 // Job tables reach device memory as kernel parameters (copied by the launch itself), so no host
-// staging buffer is needed: each launch carries up to ~30 KB of jobs.
+// staging buffer is needed: each launch carries up to ~30 KB of jobs.  CTA q copies job q, and for
+// a call of more than one job also writes the chunk -> job map over its job's chunk range
+// [chunk0_q, chunk0_{q+1}) (behind the whole job table: job_table_bytes).
 template <class T, int N>
 struct UploadBatch {
   T items[N];
-  int count;
+  int count;          // jobs in this launch
+  int first;          // index of items[0] in the call's job table
+  int njobs;          // jobs in the call
+  int64_t end_chunk;  // first chunk after the launch's last job
 };
 
 template <class T, int N>
-__global__ void upload_kernel(const __grid_constant__ UploadBatch<T, N> b, T* dst) {
+__global__ void upload_kernel(const __grid_constant__ UploadBatch<T, N> b, T* table) {
   static_assert(sizeof(T) % 4 == 0, "job size");
-  const uint32_t* src = reinterpret_cast<const uint32_t*>(b.items);
-  uint32_t* d = reinterpret_cast<uint32_t*>(dst);
-  for (int i = threadIdx.x; i < int(b.count * sizeof(T) / 4); i += blockDim.x) d[i] = src[i];
+  const int q = blockIdx.x;
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(&b.items[q]);
+  uint32_t* d = reinterpret_cast<uint32_t*>(table + b.first + q);
+  for (int i = threadIdx.x; i < int(sizeof(T) / 4); i += blockDim.x) d[i] = src[i];
+  if (b.njobs > 1) {
+    int32_t* map = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(table) + job_structs_bytes<T>(b.njobs));
+    const int64_t c0 = b.items[q].chunk0, c1 = q + 1 < b.count ? b.items[q + 1].chunk0 : b.end_chunk;
+    for (int64_t c = c0 + threadIdx.x; c < c1; c += blockDim.x) map[c] = b.first + q;
+  }
 }
 
 // ---- host side ------------------------------------------------------------------------------
@@ -255,15 +257,19 @@ int check_launch(const char* what);
 void count_launch(int n = 1);
 int set_max_smem(const void* func, int bytes);
 
-// Copy `count` host structs to device memory at dev, on stream s, through kernel parameters, and
-// (for more than one job) build the chunk -> job map behind them (job_table_bytes).
+// Copy `count` host structs to device memory at dev, on stream s, through kernel parameters, with
+// the chunk -> job map behind them for more than one job (job_table_bytes): one launch per ~30 KB
+// of jobs.
 template <class T, int N>
-int upload_batches(const T* host, int count, T* dev, cudaStream_t s) {
+int upload_batches(const T* host, int count, T* dev, int64_t total_chunks, cudaStream_t s) {
   for (int i = 0; i < count; i += N) {
     UploadBatch<T, N> b;
     b.count = count - i < N ? count - i : N;
+    b.first = i;
+    b.njobs = count;
+    b.end_chunk = i + b.count < count ? host[i + b.count].chunk0 : total_chunks;
     for (int q = 0; q < b.count; ++q) b.items[q] = host[i + q];
-    upload_kernel<T, N><<<1, 256, 0, s>>>(b, dev + i);
+    upload_kernel<T, N><<<unsigned(b.count), 256, 0, s>>>(b, dev);
     count_launch();
     if (int rc = check_launch("upload_kernel")) return rc;
   }
@@ -272,17 +278,11 @@ int upload_batches(const T* host, int count, T* dev, cudaStream_t s) {
 
 template <class T>
 int upload_jobs(const T* host, int count, T* dev, int64_t total_chunks, cudaStream_t s) {
-  // Batches of up to ~30 KB of kernel parameters; a call with a few jobs (one tensor) takes a
-  // small parameter block instead, since the launch cost grows with the block's size.
+  // A call with a few jobs (one tensor) takes a small parameter block, since the launch cost
+  // grows with the block's size.
   constexpr int N = 30000 / int(sizeof(T)) > 0 ? 30000 / int(sizeof(T)) : 1;
-  const int rc = count <= 4 ? upload_batches<T, 4>(host, count, dev, s) : upload_batches<T, N>(host, count, dev, s);
-  if (rc) return rc;
-  if (count > 1 && total_chunks > 0) {
-    map_jobs_kernel<T><<<unsigned(count), 256, 0, s>>>(dev, count, total_chunks);
-    count_launch();
-    if (int rc = check_launch("map_jobs_kernel")) return rc;
-  }
-  return ZN_OK;
+  return count <= 4 ? upload_batches<T, 4>(host, count, dev, total_chunks, s)
+                    : upload_batches<T, N>(host, count, dev, total_chunks, s);
 }
 
 // An NVTX range over a scope of host code (entry points), visible to Nsight tools.
