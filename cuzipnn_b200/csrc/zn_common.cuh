@@ -249,6 +249,23 @@ __global__ void upload_kernel(const __grid_constant__ UploadBatch<T, N> b, T* ta
   }
 }
 
+// The one job of a single-job call, passed by value to the call's first kernel, which stores it
+// into the job table for the kernels after it: such a call needs no upload launch.  valid = 0 when
+// the table was uploaded.
+template <class T>
+struct FirstJob {
+  T job;
+  int valid;
+};
+
+// Store a job into its table slot, with the threads of one CTA.
+template <class T>
+__device__ __forceinline__ void store_job(const T& job, T* slot) {
+  const uint32_t* s = reinterpret_cast<const uint32_t*>(&job);
+  uint32_t* d = reinterpret_cast<uint32_t*>(slot);
+  for (int i = threadIdx.x; i < int(sizeof(T) / 4); i += blockDim.x) d[i] = s[i];
+}
+
 // ---- host side ------------------------------------------------------------------------------
 
 // Records the error of the last failing call of this thread and returns its status.

@@ -759,10 +759,15 @@ constexpr int kScanThreads = 1024;
 // One CTA per job.  It first zeroes the job's status word.  A job whose n_comp is negative reads
 // it from the blob's header (u32 at byte 12) here; tables that do not fit the blob then mark every
 // unit invalid (the decoder zero-fills them) and set kErrTable.
-__global__ void __launch_bounds__(kScanThreads) dscan_kernel(const DecArgs* __restrict__ jobs) {
+// The first kernel of a call: a single-job call passes its job by value (`one`), which CTA 0 also
+// stores into the table at `table` for the kernels after this one.
+__global__ void __launch_bounds__(kScanThreads) dscan_kernel(const DecArgs* __restrict__ jobs,
+                                                             const __grid_constant__ FirstJob<DecArgs> one,
+                                                             DecArgs* table) {
   __shared__ int64_t sm[64];
   __shared__ int64_t s_ncomp;
-  const DecArgs& a = jobs[blockIdx.x];
+  if (one.valid && blockIdx.x == 0) store_job(one.job, table);
+  const DecArgs& a = one.valid ? one.job : jobs[blockIdx.x];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   if (tid == 0) {
     *a.status = 0;
@@ -967,10 +972,17 @@ int zn_decompress_batch(int njobs, const void* const* blobs, const int64_t* blob
   if (nj == 0) return ZN_OK;
   if (chunk0 > 0x7FFFFFFF) return set_error(ZN_ERR_INVALID, "zn_decompress: too many chunks");
   DecArgs* dj = reinterpret_cast<DecArgs*>(tb);
-  if (int rc = upload_jobs(jobs.data(), nj, dj, chunk0, s)) return rc;
+  // A single job goes to the scan kernel by value (it stores the table itself).
+  FirstJob<DecArgs> fj{};
+  if (nj == 1) {
+    fj.job = jobs[0];
+    fj.valid = 1;
+  } else if (int rc = upload_jobs(jobs.data(), nj, dj, chunk0, s)) {
+    return rc;
+  }
   {
     TimedLaunch tl("dscan", s);
-    dscan_kernel<<<unsigned(nj), kScanThreads, 0, s>>>(dj);
+    dscan_kernel<<<unsigned(nj), kScanThreads, 0, s>>>(dj, fj, dj);
   }
   count_launch();
   if (int rc = check_launch("dscan_kernel")) return rc;

@@ -304,12 +304,17 @@ __device__ __forceinline__ int64_t hist_vectors(const uint8_t* xc, int64_t m, ui
 }
 
 // Part `blockIdx.y` of chunk `blockIdx.x`: histograms of all K planes of its elements, written as
-// one partial histogram per plane (no global atomics; the encoder sums the parts).
+// one partial histogram per plane (no global atomics; the encoder sums the parts).  The first
+// kernel of a call: a single-job call passes its job by value (`one`), and CTA (0, 0) stores it
+// into the table at `table` for the kernels after this one.
 template <int K, bool REORDER>
-__global__ void __launch_bounds__(kHistThreads) hist_kernel(const EncArgs* __restrict__ jobs, int njobs) {
+__global__ void __launch_bounds__(kHistThreads) hist_kernel(const EncArgs* __restrict__ jobs, int njobs,
+                                                           const __grid_constant__ FirstJob<EncArgs> one,
+                                                           EncArgs* table) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem_raw);  // K <= 2: kHist32Bytes layout; else [K][256][kCols]
-  const EncArgs& a = jobs[find_job(jobs, njobs, blockIdx.x)];
+  if (one.valid && blockIdx.x == 0 && blockIdx.y == 0) store_job(one.job, table);
+  const EncArgs& a = one.valid ? one.job : jobs[find_job(jobs, njobs, blockIdx.x)];
   const int64_t j = blockIdx.x - a.chunk0;
   const int part = blockIdx.y, tid = threadIdx.x;
   const uint8_t* xc;
@@ -1234,14 +1239,19 @@ void bind_scratch(EncArgs& a, uint8_t* region, int64_t units) {
 }
 
 template <int K, bool REORDER>
-int launch_encode(const EncArgs* jobs, int njobs, int64_t grid, cudaStream_t s) {
+int launch_encode(EncArgs* jobs, int njobs, int64_t grid, cudaStream_t s, const EncArgs* one = nullptr) {
   if (grid <= 0) return ZN_OK;
   const size_t hs = hist_smem(K);
   auto hf = hist_kernel<K, REORDER>;
   if (int rc = set_max_smem(reinterpret_cast<const void*>(hf), int(hs))) return rc;
+  FirstJob<EncArgs> fj{};
+  if (one) {
+    fj.job = *one;
+    fj.valid = 1;
+  }
   {
     TimedLaunch tl("hist", s);
-    hf<<<dim3(unsigned(grid), kHistParts), kHistThreads, hs, s>>>(jobs, njobs);
+    hf<<<dim3(unsigned(grid), kHistParts), kHistThreads, hs, s>>>(jobs, njobs, fj, jobs);
   }
   const size_t sm = enc_smem(K);
   auto fn = encode_kernel<K, REORDER>;
@@ -1386,15 +1396,18 @@ int zn_compress_batch(int njobs, const void* const* x, const int64_t* n, int k, 
   }
   if (chunk0 > 0x7FFFFFFF / kPackParts) return set_error(ZN_ERR_INVALID, "zn_compress: too many chunks");
   EncArgs* dj = reinterpret_cast<EncArgs*>(tb);
-  if (int rc = upload_jobs(jobs.data(), njobs, dj, chunk0, s)) return rc;
+  // A single job with chunks goes to the histogram kernel by value (it stores the table itself).
+  const EncArgs* one = njobs == 1 && chunk0 > 0 ? jobs.data() : nullptr;
+  if (!one)
+    if (int rc = upload_jobs(jobs.data(), njobs, dj, chunk0, s)) return rc;
   int rc = ZN_OK;
   switch (k * 2 + (reorder ? 1 : 0)) {
-    case 2: rc = launch_encode<1, false>(dj, njobs, chunk0, s); break;
-    case 4: rc = launch_encode<2, false>(dj, njobs, chunk0, s); break;
-    case 5: rc = launch_encode<2, true>(dj, njobs, chunk0, s); break;
-    case 8: rc = launch_encode<4, false>(dj, njobs, chunk0, s); break;
-    case 9: rc = launch_encode<4, true>(dj, njobs, chunk0, s); break;
-    default: rc = launch_encode<8, false>(dj, njobs, chunk0, s); break;
+    case 2: rc = launch_encode<1, false>(dj, njobs, chunk0, s, one); break;
+    case 4: rc = launch_encode<2, false>(dj, njobs, chunk0, s, one); break;
+    case 5: rc = launch_encode<2, true>(dj, njobs, chunk0, s, one); break;
+    case 8: rc = launch_encode<4, false>(dj, njobs, chunk0, s, one); break;
+    case 9: rc = launch_encode<4, true>(dj, njobs, chunk0, s, one); break;
+    default: rc = launch_encode<8, false>(dj, njobs, chunk0, s, one); break;
   }
   if (rc) return rc;
   {
