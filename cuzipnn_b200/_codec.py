@@ -382,13 +382,13 @@ def _compress(
     with _on(device):
         if not x.is_cuda:
             x = _upload(x.contiguous(), device)
-        elif not (x.device == device and x.is_contiguous()):
+        elif not (x.get_device() == device.index and x.is_contiguous()):
             x = x.to(device, non_blocking=True, memory_format=torch.contiguous_format).contiguous()
-        x = x.view(-1)
-        if x.data_ptr() % 16:
+        if x.data_ptr() % 16:  # only the address and the size of the contiguous input are used
             x = x.clone()
-        head = _header(tensor, _FLAG_REORDER if reorder else 0, chunk_bytes, 0)
-        cap = int(_lib.lib.zn_compress_bound(n, k, tensor.dim(), chunk_bytes))
+        shape = tuple(tensor.shape)
+        head = _header_bytes(x.dtype, shape, _FLAG_REORDER if reorder else 0, chunk_bytes, 0)
+        cap = int(_lib.lib.zn_compress_bound(n, k, len(shape), chunk_bytes))
         temp_bytes = int(_lib.lib.zn_compress_temp_bytes(n, k, chunk_bytes, sub_chunks))
         # The blob is packed into a buffer at least as large as the input (README "API").
         out = torch.empty(cap, dtype=torch.uint8, device=device)
@@ -408,8 +408,7 @@ def _compress(
         if checksum_chunk_bytes is not None:
             crc = _crc32(comp, checksum_chunk_bytes)
         if not readback_to_cpu:
-            return _remember(comp, tensor.dtype, tuple(tensor.shape), _FLAG_REORDER if reorder else 0, chunk_bytes,
-                             n), crc
+            return _remember(comp, tensor.dtype, shape, _FLAG_REORDER if reorder else 0, chunk_bytes, n), crc
         if pin_memory:
             blob = _populated_empty(size, pin_memory=True)
             # With a crc, crc.cpu() below syncs the stream, so blob is complete on return.
